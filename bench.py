@@ -1,0 +1,437 @@
+#!/usr/bin/env python
+"""Decode benchmark (the reference's `voltattn --bench`, src/voltattn.cu:967-1070,
+re-derived for B200) with the driver's JSON contract.
+
+A step is one batch-1 attention decode over all H=32 heads, D=128, L=16384
+in format --fmt (default q4+), through the C ABI. The KV
+cache is synthetic: fp32 N(0,1) K/V drawn on the GPU from a seeded generator
+and packed by the GPU quantizer; q is fp16 N(0,1). Rank r of N decodes its own
+sequence (weak scaling, no collective on the data path).
+
+Timing: W warm-up steps plus a ~0.3 s soak, then exactly K steps replayed from
+CUDA graphs, bracketed by barrier + synchronize; CUDA events on the launching
+stream; max over ranks. Each step reads a different copy of the cache from a
+rotation whose total exceeds 4x the L2 size, so L2 cannot serve the stream.
+
+`--impl reference` times the reference's own CPU path (reference() of
+src/voltattn.cu:769-794 over the dequantized cache, all host threads, built
+from the reference source into oracle/_ref) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, D = 32, 128
+FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the top kernel,
+# from the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_BYTES = {}
+
+
+def algorithmic_bytes(fmt: str, L: int) -> int:
+    """K+V payload + fp16 group scales, q/out/workspace excluded
+    (src/voltattn.cu:989-992)."""
+    n = H * L * D
+    bits = FORMAT_BITS[fmt]
+    payload = 2 * n if bits == 16 else n if bits == 8 else n // 2 if bits == 4 else n * 3 // 8
+    scales = 0 if bits == 16 else H * L * (D // 64) * 2
+    return 2 * (payload + scales)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--fmt", default="q4+")
+    ap.add_argument("--L", type=int, default=16384)
+    ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+",
+                    help="formats also timed for the per-format table (empty: none)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- helpers ----
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return json.load(fh), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms."""
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+               "--format=csv,noheader,nounits", "-lms", "50"]
+        if self.uuid:
+            cmd += ["-i", self.uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.th.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample_plan(t_full: float, K: int, budget_s: float):
+    """Fraction of the full decode one CPU step covers so that K steps take
+    about budget_s: whole heads while that is enough, else a prefix of the
+    positions of one head."""
+    frac = min(1.0, budget_s / max(1e-9, K * t_full))
+    heads = max(1, min(H, int(math.floor(frac * H))))
+    if frac * H >= 1.0:
+        return heads, None
+    return 1, max(64, int(frac * H * 1.0 * 16384))
+
+
+# ------------------------------------------------------------ CPU paths -------
+
+def cpu_reference_setup(L: int, fmt: str, seed: int = 1234):
+    """The reference's CPU decode inputs: exactly dequantized K/V (fp32) and
+    fp16 q, quantized by the reference's own quantize() where built."""
+    from oracle.oracle import REF_SO, Oracle, RefLib
+    o = Oracle()
+    kind = "reference" if os.path.exists(REF_SO) else "port"
+    lib = RefLib() if kind == "reference" else o
+    rng = np.random.default_rng(seed)
+    kx = rng.standard_normal(H * L * D, dtype=np.float32)
+    vx = rng.standard_normal(H * L * D, dtype=np.float32)
+    q = o.f2h(rng.standard_normal(H * D, dtype=np.float32))
+    bits = FORMAT_BITS[fmt]
+    if bits == 16:
+        kd, vd = o.round_to_half(kx), o.round_to_half(vx)
+    else:
+        kc, ks = lib.quantize(kx, H, L, D, bits)
+        vc, vs = lib.quantize(vx, H, L, D, bits)
+        kd, vd = lib.dequant(kc, ks, H, L, D, bits), lib.dequant(vc, vs, H, L, D, bits)
+    return lib, kind, kd, vd, q
+
+
+def cpu_time_step(lib, kd, vd, q, L, heads, positions, threads):
+    if positions is None:
+        n = heads * L * D
+        t = time.perf_counter()
+        lib.reference(kd[:n], vd[:n], q[:heads * D], heads, L, D, threads=threads)
+        return time.perf_counter() - t, heads / H
+    kh = np.ascontiguousarray(kd[:L * D].reshape(L, D)[:positions])
+    vh = np.ascontiguousarray(vd[:L * D].reshape(L, D)[:positions])
+    t = time.perf_counter()
+    lib.reference(kh, vh, q[:D], 1, positions, D, threads=1)
+    return time.perf_counter() - t, positions / (H * L)
+
+
+def cpu_baseline_leg(L, fmt):
+    threads = os.cpu_count() or 1
+    lib, kind, kd, vd, q = cpu_reference_setup(L, fmt)
+    t_full, _ = cpu_time_step(lib, kd, vd, q, L, H, None, threads)
+    runs = max(1, min(200, int(10.0 / max(t_full, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(runs):
+        cpu_time_step(lib, kd, vd, q, L, H, None, threads)
+    dt = time.perf_counter() - t0
+    return {"value": runs / dt, "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": f"{runs} full decodes (H={H}, D={D}, L={L}, {fmt} cache dequantized to fp32 by the "
+                      f"reference's dq), heads over {threads} threads, double-precision reference()"}
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    L, fmt = args.L, args.fmt
+    threads = os.cpu_count() or 1
+    lib, kind, kd, vd, q = cpu_reference_setup(L, fmt)
+    t_full, _ = cpu_time_step(lib, kd, vd, q, L, H, None, threads)
+    heads, positions = cpu_sample_plan(t_full, args.steps + args.warmup, 120.0)
+    for _ in range(args.warmup):
+        cpu_time_step(lib, kd, vd, q, L, heads, positions, threads)
+    total, covered = 0.0, 0.0
+    for _ in range(args.steps):
+        dt, frac = cpu_time_step(lib, kd, vd, q, L, heads, positions, threads)
+        total += dt
+        covered += frac
+    value = covered / total  # full decodes per second
+    sample = (f"each step: {heads} of {H} heads, all {L} positions" if positions is None else
+              f"each step: 1 head, first {positions} of {L} positions") + \
+        f"; {fmt} cache dequantized by the reference's dq; reference() on {threads if positions is None else 1} threads"
+    line = {"impl": "reference", "metric": f"decode tok/s (batch 1, H={H}, D={D}, L={L}, {fmt})",
+            "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64", "data": "synthetic: fp32 N(0,1) K/V, fp16 N(0,1) q, seeded",
+            "config": {"workload": f"batch-1 decode H={H} D={D} L={L} fmt={fmt}", "H": H, "D": D, "L": L,
+                       "fmt": fmt},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads if positions is None else 1,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU path --------
+
+def make_cache(va, torch, fmt, L, seed, dev):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    n = H * L * D
+    kx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
+    vx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
+    bits = FORMAT_BITS[fmt]
+    if bits == 16:
+        K, V, sK, sV = kx.half(), vx.half(), None, None
+    else:
+        K, sK = va.quantize(kx, bits, H, L, D)
+        V, sV = va.quantize(vx, bits, H, L, D)
+    del kx, vx
+    return K, V, sK, sV
+
+
+def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3):
+    """Returns (ms_per_step, S, copies, launches_per_step) for K_steps decodes."""
+    nbytes = algorithmic_bytes(fmt, L)
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
+    copies = max(2, math.ceil(4 * l2 / nbytes))
+    base = make_cache(va, torch, fmt, L, seed, dev)
+    caches = [base] + [tuple(None if t is None else t.clone() for t in base) for _ in range(copies - 1)]
+    q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 1)).half()
+    out = torch.empty(H * D, dtype=torch.float16, device=dev)
+    S = va.suggest_splits(fmt, H, L, D)
+    ws = va.new_workspace(H, D, S, dev)
+    bufs = [va.DeviceBufs(*c, q, out, ws) for c in caches]
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(i):
+        va.launch(fmt, bufs[i % copies], H, L, D, S, stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(3, W)):
+            step(i)
+    torch.cuda.synchronize(dev)
+    chunk = min(K_steps, 32 * copies)
+    graphs = []
+
+    def capture(n):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            for i in range(n):
+                step(i)
+        return gph
+
+    main = capture(chunk)
+    reps, tail = divmod(K_steps, chunk)
+    tail_g = capture(tail) if tail else None
+    torch.cuda.synchronize(dev)
+    # soak (untimed): same work, lets clocks settle for the sampler
+    t_end = time.perf_counter() + soak_s
+    while time.perf_counter() < t_end:
+        main.replay()
+        torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            main.replay()
+        if tail_g is not None:
+            tail_g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = 1 if fmt.endswith("+") else 2
+    del graphs
+    return ms / K_steps, S, copies, launches
+
+
+def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
+    """End to end through the public API: per step, H2D of q from pinned host
+    memory, decode, D2H of the fp16 output, synchronize."""
+    K, V, sK, sV = make_cache(va, torch, fmt, L, seed, dev)
+    S = va.suggest_splits(fmt, H, L, D)
+    ws = va.new_workspace(H, D, S, dev)
+    nq = 64
+    q_host = torch.randn(nq, H * D).half().pin_memory()
+    out_host = torch.empty(nq, H * D, dtype=torch.float16).pin_memory()
+    q = torch.empty(H * D, dtype=torch.float16, device=dev)
+    out = torch.empty(H * D, dtype=torch.float16, device=dev)
+    b = va.DeviceBufs(K, V, sK, sV, q, out, ws)
+    stream = torch.cuda.Stream(device=dev)
+    steps = min(K_steps, 20000)
+
+    def one(i):
+        with torch.cuda.stream(stream):
+            q.copy_(q_host[i % nq], non_blocking=True)
+            va.launch(fmt, b, H, L, D, S, stream)
+            out_host[i % nq].copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(5):
+        one(i)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        one(i)
+    dt = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([dt], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    n = dist.get_world_size() if dist else 1
+    return {"value": n * steps / dt, "unit": "tok/s", "h2d_bytes_per_step": H * D * 2,
+            "d2h_bytes_per_step": H * D * 2, "steps": steps,
+            "note": "KV cache resident in HBM (decode state); per step q in, output out, sync"}
+
+
+def run_ours(args, rank, world):
+    import torch
+    import voltattn_b200 as va
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", device_id=dev)
+        dist = tdist
+    peaks, peaks_kind = measured_peaks()
+    fmt, L, K, W = args.fmt, args.L, args.steps, args.warmup
+    seed = 1234 + 7919 * rank
+    probe = va.probe_ceiling(local, nbytes=4 << 30, reps=10)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = None
+
+    table = {}
+    for f in [x for x in args.table.split(",") if x]:
+        if f == fmt:
+            continue
+        steps_f = max(200, min(K, 5000))
+        ms, S_f, copies_f, _ = time_format(va, torch, f, L, steps_f, W, dev, dist, seed, soak_s=0.05)
+        gbs = algorithmic_bytes(f, L) / (ms * 1e6)
+        table[f] = {"ms": ms, "gbs": gbs, "mbu_probe": gbs / probe, "tok_s": 1e3 / ms, "splits": S_f}
+        torch.cuda.empty_cache()
+
+    with ClockSampler(uuid) as clk:
+        ms, S, copies, launches = time_format(va, torch, fmt, L, K, W, dev, dist, seed)
+    clocks = clk.summary()
+    nbytes = algorithmic_bytes(fmt, L)
+    gbs = nbytes / (ms * 1e6)
+    table[fmt] = {"ms": ms, "gbs": gbs, "mbu_probe": gbs / probe, "tok_s": 1e3 / ms, "splits": S}
+    base = table.get("f16+")
+    for f, r in table.items():
+        if base:
+            r["vs_f16+"] = base["ms"] / r["ms"]
+        if "f16" in table:
+            r["vs_f16"] = table["f16"]["ms"] / r["ms"]
+    torch.cuda.empty_cache()
+    e2e = e2e_leg(va, torch, fmt, L, K, dev, dist, seed)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_leg(L, fmt)
+    if rank == 0:
+        value = world * 1e3 / ms
+        traffic = NCU_TRAFFIC_BYTES.get(fmt)
+        line = {
+            "metric": f"decode tok/s (batch 1, H={H}, D={D}, L={L}, {fmt}); MBU vs probed read ceiling",
+            "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: fp32 N(0,1) K/V drawn on the GPU from a seed and packed by the GPU quantizer; "
+                    "fp16 N(0,1) q",
+            "config": {"workload": f"batch-1 decode H={H} D={D} L={L} fmt={fmt}", "H": H, "D": D, "L": L,
+                       "fmt": fmt, "splits": S, "parallelism": f"weak: one sequence per GPU x{world}",
+                       "l2": f"rotating {copies} cache copies ({copies * nbytes / 1e6:.0f} MB > 4x L2)",
+                       "timing": "CUDA graphs of back-to-back decodes, CUDA events on the launch stream"},
+            "impl": "ours",
+            "mbu_probe": gbs / probe, "probe_gbs": probe,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_kind": f"{peaks_kind} (copy bandwidth, MEASURED_PEAKS.json)",
+                         "algorithmic_bytes_per_launch": nbytes},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": K * launches,
+            "clocks": clocks,
+            "formats": table,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    run_ours(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * voltattn_b200 — C ABI of the B200 (sm_100a) fused dequant + online-softmax
+ * attention decode path.
+ *
+ * The reference (kamilch1k/voltattn, one CUDA C++ file src/voltattn.cu) has no
+ * library or FFI; its host interface is the internal C++ surface this header
+ * replaces entry by entry (citations are src/voltattn.cu:line):
+ *
+ *   enum class Fmt / fmt_name            :676-686  -> va_fmt, va_fmt_name, va_fmt_from_name
+ *   struct DeviceBufs                    :796-801  -> va_bufs (+ explicit workspace argument)
+ *   launch(Fmt, DeviceBufs, H, L, D, S)  :803-835  -> va_decode
+ *   combine<<<H,128>>>                   :651-672  -> va_combine_partials
+ *   quantize(x, H, L, D, bits)           :705-745  -> va_quantize (a GPU kernel, bit-exact)
+ *   probe_ceiling()                      :935-957  -> va_probe_ceiling
+ *   CUDA_CHECK -> exit(1)                :49-58    -> status codes, va_status_string
+ *
+ * Conventions: every entry point returns a va_status (0 = success) and never
+ * exits the process. Pointers are device pointers owned by the caller unless
+ * stated otherwise. `stream` is a cudaStream_t passed as void* (NULL = the
+ * legacy default stream, as the reference uses). Launches are asynchronous
+ * with respect to the host, like the reference's launch().
+ *
+ * Data layout (identical to the reference, src/voltattn.cu:189, :254, :494,
+ * :563, :694-703): K and V are head-major [H][L][D] rows.
+ *   f16 formats : __half [H][L][D]
+ *   q8          : int8   [H][L][D], code v in [-127,127]
+ *   q4          : uint8  [H][L][D/2], byte k holds dims 2k (low nibble) and
+ *                 2k+1 (high nibble), nibble = v + 8, v in [-7,7]
+ *   q3          : uint8  [H][L][3D/8], element e of a row-major tensor sits at
+ *                 bits 3*(e%8) of the little-endian 3-byte granule e/8, field = v+4
+ *   scales      : __half [H][L][D/64] symmetric per-group scales (group = 64
+ *                 consecutive dims), absent (NULL) for the f16 formats
+ *   q, out      : __half [H][D]
+ * D must be 64 or 128. K, V, scK, scV must be 16-byte aligned (cudaMalloc
+ * and the torch allocator give 256).
+ */
+#ifndef VOLTATTN_B200_H
+#define VOLTATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VA_API __attribute__((visibility("default")))
+#else
+#define VA_API
+#endif
+
+/* Formats, in the reference's order (src/voltattn.cu:676). The "+" formats run
+ * the staged streaming kernel; f16 / q8 / q4 run the plain one-warp-per-position
+ * kernel family kept as attribution baselines. */
+typedef enum va_fmt {
+    VA_F16 = 0,
+    VA_F16P = 1,
+    VA_Q8 = 2,
+    VA_Q8P = 3,
+    VA_Q4 = 4,
+    VA_Q4P = 5,
+    VA_Q3P = 6
+} va_fmt;
+
+typedef enum va_status {
+    VA_OK = 0,
+    VA_ERR_INVALID = 1,     /* bad format, shape or null pointer */
+    VA_ERR_ALIGN = 2,       /* a K/V/scale pointer is not 16-byte aligned */
+    VA_ERR_WORKSPACE = 3,   /* workspace missing or smaller than required */
+    VA_ERR_CUDA = 4,        /* a CUDA runtime call failed (see va_last_cuda_error) */
+    VA_ERR_UNSUPPORTED = 5, /* D or format not supported by this build */
+    VA_ERR_DEVICE = 6,      /* a kernel reported a device-side error (va_device_error) */
+    VA_ERR_TOO_LARGE = 7    /* size beyond a stated maximum */
+} va_status;
+
+/* DeviceBufs (src/voltattn.cu:796-801) without `ws`, which every entry point
+ * takes explicitly together with its size. */
+typedef struct va_bufs {
+    const void* K;
+    const void* V;
+    const void* scK; /* NULL for f16 formats */
+    const void* scV; /* NULL for f16 formats */
+    const void* q;   /* __half [H][D] */
+    void* out;       /* __half [H][D] */
+} va_bufs;
+
+/* Library version as 10000*major + 100*minor + patch. No reference counterpart. */
+VA_API int va_version(void);
+
+/* fmt_name (src/voltattn.cu:677-686): "f16", "f16+", "q8", "q8+", "q4", "q4+",
+ * "q3+" (without the reference's padding blanks); NULL for an invalid value. */
+VA_API const char* va_fmt_name(int fmt);
+/* Inverse of va_fmt_name; -1 when unknown. */
+VA_API int va_fmt_from_name(const char* name);
+/* Quantization bits of a format: 16, 8, 4 or 3 (qbits, src/voltattn.cu:691). */
+VA_API int va_fmt_bits(int fmt);
+/* Payload bytes of n elements (qbytes, src/voltattn.cu:692; 2n for f16). */
+VA_API size_t va_payload_bytes(int fmt, size_t n);
+/* Human-readable text of a va_status. */
+VA_API const char* va_status_string(int status);
+/* The cudaError_t of the last failing CUDA call made by this library on the
+ * calling thread (0 if none). */
+VA_API int va_last_cuda_error(void);
+
+/* Workspace bytes va_decode needs for (H, D, S): the reference's H*S*(D+2)
+ * floats of split partials (src/voltattn.cu:888) followed by one completion
+ * counter per head. The counters must be zero before the first call (allocate
+ * with cudaMemset / torch.zeros or call va_workspace_init); every completed
+ * call leaves them zero again, so one workspace serves any number of calls
+ * issued in order on one stream. */
+VA_API size_t va_workspace_bytes(int H, int D, int S);
+/* Zeroes a workspace of `bytes` bytes on `stream`. */
+VA_API int va_workspace_init(void* ws, size_t bytes, void* stream);
+
+/* A split count S for (fmt, H, L, D) that balances the persistent grid of the
+ * current device (whole waves of work units); the reference's bench rule
+ * (src/voltattn.cu:1026) is tuned for an 80-SM V100. Writes *S. */
+VA_API int va_suggest_splits(int fmt, int H, int L, int D, int* S);
+
+/* One batch-1 decode step over all H heads (launch, src/voltattn.cu:803-835):
+ *   out[h] = softmax_j(q[h] . K[h][j] / sqrt(D)) . V[h][j]   (fp16 out, fp32 math)
+ * with K/V dequantized in registers. S = number of KV-length splits per head
+ * (1 <= S <= 65535); positions of head h are split into S contiguous ranges,
+ * each producing an (m, l, o) partial merged by a log-sum-exp combine.
+ * ws_bytes >= va_workspace_bytes(H, D, S): one launch, the combine fused into
+ * the last CTA of each head. ws_bytes >= H*S*(D+2)*4 only (the reference's
+ * workspace size): two launches, decode then combine. */
+VA_API int va_decode(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes,
+                     void* stream);
+
+/* Split-L building block for multi-GPU decode (no reference counterpart; the
+ * reference is single-GPU). As va_decode, but instead of fp16 output writes
+ * each head's merged partial to `partial` = float [H][D+2] laid out like a
+ * reference workspace slot (src/voltattn.cu:92-93): m (max scaled score, natural
+ * log units), l (sum of exp(score - m)), o[D] (sum of exp(score - m) * V).
+ * Requires ws_bytes >= va_workspace_bytes(H, D, S). */
+VA_API int va_decode_partial(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws,
+                             size_t ws_bytes, float* partial, void* stream);
+
+/* Log-sum-exp merge (combine, src/voltattn.cu:651-672) of R*S slots per head:
+ * slots = float [R][H][S][D+2] (R = 1 is the reference's workspace layout; R > 1
+ * is R gathered va_decode_partial / workspace blocks, e.g. one per GPU).
+ * Writes fp16 out [H][D]. */
+VA_API int va_combine_partials(const float* slots, int R, int H, int S, int D, void* out, void* stream);
+
+/* Symmetric per-group quantizer (quantize, src/voltattn.cu:705-745) as a GPU
+ * kernel, bit-exact with the reference's host function: for every 64-element
+ * group of x (fp32 [H][L][D]) s = amax/lim (lim 127/7/3 for bits 8/4/3) is
+ * rounded to fp16, and each code is round-half-even(x / stored scale) clamped
+ * to [-lim, lim], packed as in the layout above. codes: va_payload_bytes
+ * bytes; scales: __half [H][L][D/64]. x must be 16-byte aligned. */
+VA_API int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
+                       void* stream);
+
+/* Read-bandwidth ceiling of `device` (probe_ceiling, src/voltattn.cu:935-957),
+ * re-derived for HBM3e: streams a `bytes`-byte buffer (0 = 4 GiB) `reps` times
+ * (0 = 20) after 3 warm-up passes with each of two kernels (wide vector loads;
+ * bulk asynchronous copies into shared memory) and writes the best GB/s
+ * (1e9 bytes/s) to *gbs. Allocates and frees its own buffer. Synchronous. */
+VA_API int va_probe_ceiling(int device, size_t bytes, int reps, double* gbs);
+/* The same for one method (0 = vector loads, 1 = bulk copies); *gbs = best. */
+VA_API int va_probe_ceiling_method(int device, int method, size_t bytes, int reps, double* gbs);
+
+/* Batched grouped-query decode with per-sequence lengths (no reference
+ * counterpart; the reference is batch 1, one KV head per query head).
+ * K/V: [B][Hkv][Lmax][D] rows in format fmt (rows >= lens[b] are never read),
+ * scales [B][Hkv][Lmax][D/64]; q, out: __half [B][Hq][D]; lens: device int32
+ * [B], 1 <= lens[b] <= Lmax. Query head hq reads KV head hq / (Hq / Hkv).
+ * Each (sequence, KV head) streams its cache once for all of its query heads.
+ * S = max splits per sequence; ws_bytes >= va_gqa_workspace_bytes(...). */
+VA_API size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S);
+VA_API int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax,
+                         int D, int S, void* ws, size_t ws_bytes, void* stream);
+
+/* Device-side error word (bounded waits that gave up, etc.). Reads and clears
+ * the flag of the current device; *code = 0 when no kernel reported one. */
+VA_API int va_device_error(int* code);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* VOLTATTN_B200_H */

@@ -1,0 +1,258 @@
+"""voltattn_b200 — B200-native fused dequant + online-softmax attention decode.
+
+Python mirror of the reference's host interface (kamilch1k/voltattn,
+src/voltattn.cu) over the C ABI in include/voltattn.h, loaded with ctypes from
+the in-tree libvoltattn_b200.so. Device memory, streams and
+torch.distributed come from PyTorch; all compute runs in this package's CUDA
+kernels. There is no CPU fallback: importing the package fails loudly when the
+shared library is missing.
+
+Reference names kept: `Fmt` (:676), `fmt_name` (:677), `DeviceBufs` (:796),
+`launch` (:803), `quantize` (:709), `probe_ceiling` (:935), `GROUP` (:60),
+`qbits` / `qbytes` (:691-692).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvoltattn_b200.so")
+
+GROUP = 64
+
+
+class VoltAttnError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {_lib.va_status_string(status).decode()} (status {status}"
+                         + (f", cudaError {_lib.va_last_cuda_error()}" if status == 4 else "") + ")")
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"voltattn_b200: {LIB_PATH} is missing — build it with `make` or "
+                          "`python -c 'import __graft_entry__ as g; g.build()'` (no CPU fallback exists)")
+    lib = C.CDLL(LIB_PATH)
+    vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
+    lib.va_version.restype = i
+    lib.va_fmt_name.argtypes = [i]; lib.va_fmt_name.restype = C.c_char_p
+    lib.va_fmt_from_name.argtypes = [C.c_char_p]; lib.va_fmt_from_name.restype = i
+    lib.va_fmt_bits.argtypes = [i]; lib.va_fmt_bits.restype = i
+    lib.va_payload_bytes.argtypes = [i, sz]; lib.va_payload_bytes.restype = sz
+    lib.va_status_string.argtypes = [i]; lib.va_status_string.restype = C.c_char_p
+    lib.va_last_cuda_error.restype = i
+    lib.va_workspace_bytes.argtypes = [i, i, i]; lib.va_workspace_bytes.restype = sz
+    lib.va_workspace_init.argtypes = [vp, sz, vp]; lib.va_workspace_init.restype = i
+    lib.va_suggest_splits.argtypes = [i, i, i, i, C.POINTER(i)]; lib.va_suggest_splits.restype = i
+    lib.va_decode.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, vp, sz, vp]; lib.va_decode.restype = i
+    lib.va_decode_partial.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, vp, sz, vp, vp]
+    lib.va_decode_partial.restype = i
+    lib.va_combine_partials.argtypes = [vp, i, i, i, i, vp, vp]; lib.va_combine_partials.restype = i
+    lib.va_quantize.argtypes = [i, vp, vp, vp, i, i, i, vp]; lib.va_quantize.restype = i
+    lib.va_probe_ceiling.argtypes = [i, sz, i, C.POINTER(C.c_double)]; lib.va_probe_ceiling.restype = i
+    lib.va_probe_ceiling_method.argtypes = [i, i, sz, i, C.POINTER(C.c_double)]
+    lib.va_probe_ceiling_method.restype = i
+    lib.va_gqa_workspace_bytes.argtypes = [i, i, i, i]; lib.va_gqa_workspace_bytes.restype = sz
+    lib.va_decode_gqa.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, vp, sz, vp]
+    lib.va_decode_gqa.restype = i
+    lib.va_device_error.argtypes = [C.POINTER(i)]; lib.va_device_error.restype = i
+    return lib
+
+
+class VaBufs(C.Structure):
+    _fields_ = [("K", C.c_void_p), ("V", C.c_void_p), ("scK", C.c_void_p), ("scV", C.c_void_p),
+                ("q", C.c_void_p), ("out", C.c_void_p)]
+
+
+_lib = _load()
+
+
+def lib():
+    """The loaded ctypes library (for tests that call the C ABI directly)."""
+    return _lib
+
+
+def _check(status: int, what: str):
+    if status != 0:
+        raise VoltAttnError(status, what)
+
+
+class Fmt(enum.IntEnum):
+    """Formats in the reference's order (src/voltattn.cu:676)."""
+    F16 = 0
+    F16M = 1
+    Q8 = 2
+    Q8M = 3
+    Q4 = 4
+    Q4M = 5
+    Q3M = 6
+
+    @property
+    def name_str(self) -> str:
+        return fmt_name(self)
+
+    @classmethod
+    def parse(cls, f) -> "Fmt":
+        if isinstance(f, Fmt):
+            return f
+        if isinstance(f, int):
+            return cls(f)
+        v = _lib.va_fmt_from_name(str(f).strip().encode())
+        if v < 0:
+            raise ValueError(f"unknown format {f!r}")
+        return cls(v)
+
+
+FORMATS = [Fmt(i) for i in range(7)]
+
+
+def fmt_name(f) -> str:
+    return _lib.va_fmt_name(int(Fmt.parse(f))).decode()
+
+
+def is_f16(f) -> bool:
+    return Fmt.parse(f) in (Fmt.F16, Fmt.F16M)
+
+
+def qbits(f) -> int:
+    """Quantization bits of a quantized format (src/voltattn.cu:691)."""
+    return {Fmt.Q8: 8, Fmt.Q8M: 8, Fmt.Q4: 4, Fmt.Q4M: 4, Fmt.Q3M: 3}.get(Fmt.parse(f), 8)
+
+
+def qbytes(bits: int, n: int) -> int:
+    """Payload bytes of n codes (src/voltattn.cu:692)."""
+    return n if bits == 8 else n // 2 if bits == 4 else n * 3 // 8
+
+
+def payload_bytes(f, n: int) -> int:
+    return int(_lib.va_payload_bytes(int(Fmt.parse(f)), n))
+
+
+def workspace_bytes(H: int, D: int, S: int) -> int:
+    return int(_lib.va_workspace_bytes(H, D, S))
+
+
+def suggest_splits(f, H: int, L: int, D: int) -> int:
+    s = C.c_int(0)
+    _check(_lib.va_suggest_splits(int(Fmt.parse(f)), H, L, D, C.byref(s)), "suggest_splits")
+    return s.value
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+@dataclass
+class DeviceBufs:
+    """The reference's DeviceBufs (src/voltattn.cu:796-801) over torch tensors:
+    K, V codes (uint8 / int8 / float16), scK / scV fp16 group scales (None for
+    the f16 formats), q and out fp16 [H][D], ws float32 workspace."""
+    K: object
+    V: object
+    scK: object = None
+    scV: object = None
+    q: object = None
+    out: object = None
+    ws: object = None
+
+    def va(self) -> VaBufs:
+        return VaBufs(_ptr(self.K), _ptr(self.V), _ptr(self.scK), _ptr(self.scV), _ptr(self.q), _ptr(self.out))
+
+
+def new_workspace(H: int, D: int, S: int, device=None):
+    """A zeroed workspace for the fused single-launch decode."""
+    import torch
+    return torch.zeros(workspace_bytes(H, D, S), dtype=torch.uint8, device=device or "cuda")
+
+
+def launch(fmt, b: DeviceBufs, H: int, L: int, D: int, S: int, stream=None):
+    """One decode step (launch, src/voltattn.cu:803). With b.ws of
+    workspace_bytes(H, D, S) bytes (zeroed once) the combine is fused into the
+    decode launch; with the reference's H*S*(D+2) floats it runs as a second
+    launch. Asynchronous on `stream` (default: torch's current stream)."""
+    vb = b.va()
+    _check(_lib.va_decode(int(Fmt.parse(fmt)), C.byref(vb), H, L, D, S, _ptr(b.ws),
+                          b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)), "launch")
+
+
+def decode_partial(fmt, b: DeviceBufs, H: int, L: int, D: int, S: int, partial, stream=None):
+    """Per-head merged (m, l, o[D]) partials, float32 [H][D+2] (split-L building block)."""
+    vb = b.va()
+    _check(_lib.va_decode_partial(int(Fmt.parse(fmt)), C.byref(vb), H, L, D, S, _ptr(b.ws),
+                                  b.ws.numel() * b.ws.element_size(), _ptr(partial), _stream_ptr(stream)),
+           "decode_partial")
+
+
+def combine_partials(slots, R: int, H: int, S: int, D: int, out, stream=None):
+    """Log-sum-exp merge of float32 slots [R][H][S][D+2] into fp16 out [H][D]."""
+    _check(_lib.va_combine_partials(_ptr(slots), R, H, S, D, _ptr(out), _stream_ptr(stream)),
+           "combine_partials")
+
+
+def quantize(x, bits: int, H: int, L: int, D: int, codes=None, scales=None, stream=None):
+    """GPU group quantizer (quantize, src/voltattn.cu:709), bit-exact with the
+    reference. x: float32 CUDA tensor with H*L*D elements. Returns (codes uint8,
+    scales float16)."""
+    import torch
+    n = H * L * D
+    if x.dtype != torch.float32 or not x.is_cuda or x.numel() != n or not x.is_contiguous():
+        raise ValueError("quantize: x must be a contiguous float32 CUDA tensor of H*L*D elements")
+    if codes is None:
+        codes = torch.empty(qbytes(bits, n), dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty(H * L * (D // GROUP), dtype=torch.float16, device=x.device)
+    _check(_lib.va_quantize(bits, _ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)), "quantize")
+    return codes, scales
+
+
+def probe_ceiling(device: int = 0, nbytes: int = 0, reps: int = 0, method: Optional[int] = None) -> float:
+    """HBM read ceiling in GB/s (probe_ceiling, src/voltattn.cu:935)."""
+    g = C.c_double(0.0)
+    if method is None:
+        _check(_lib.va_probe_ceiling(device, nbytes, reps, C.byref(g)), "probe_ceiling")
+    else:
+        _check(_lib.va_probe_ceiling_method(device, method, nbytes, reps, C.byref(g)), "probe_ceiling")
+    return g.value
+
+
+def gqa_workspace_bytes(B: int, Hq: int, D: int, S: int) -> int:
+    return int(_lib.va_gqa_workspace_bytes(B, Hq, D, S))
+
+
+def decode_gqa(fmt, b: DeviceBufs, lens, B: int, Hq: int, Hkv: int, Lmax: int, D: int, S: int, stream=None):
+    """Batched grouped-query decode with per-sequence lengths (int32 CUDA tensor)."""
+    vb = b.va()
+    _check(_lib.va_decode_gqa(int(Fmt.parse(fmt)), C.byref(vb), _ptr(lens), B, Hq, Hkv, Lmax, D, S, _ptr(b.ws),
+                              b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)), "decode_gqa")
+
+
+def device_error() -> int:
+    """Reads and clears the device error word (bounded waits that gave up)."""
+    c = C.c_int(0)
+    _check(_lib.va_device_error(C.byref(c)), "device_error")
+    return c.value
+
+
+def decode(fmt, K, V, scK, scV, q, H: int, L: int, D: int, S: Optional[int] = None, out=None, ws=None,
+           stream=None):
+    """Convenience: allocates out / workspace as needed and runs one decode."""
+    import torch
+    if S is None:
+        S = suggest_splits(fmt, H, L, D)
+    if out is None:
+        out = torch.empty(H * D, dtype=torch.float16, device=q.device)
+    if ws is None:
+        ws = new_workspace(H, D, S, q.device)
+    launch(fmt, DeviceBufs(K, V, scK, scV, q, out, ws), H, L, D, S, stream)
+    return out

@@ -1,0 +1,84 @@
+// KV group quantizer / packer as a GPU kernel, bit-exact with the reference's
+// host quantize() (src/voltattn.cu:705-745):
+//   amax = max_i |x_i| over a 64-element group (nan elements ignored, as
+//          std::max(amax, fabs(nan)) keeps amax);
+//   s    = amax > 0 ? amax / lim : 1   (IEEE fp32 division), stored as fp16 (RNE);
+//   v    = (int)lrint(x / stored_scale) (IEEE division, round-half-even), then
+//          clamped to [-lim, lim]. lrint of nan / |y| >= 2^63 yields the x86-64
+//          "integer indefinite" LONG_MIN whose low 32 bits are 0; finite values
+//          narrow to int by keeping the low 32 bits — both reproduced here;
+//   packing: q8 int8; q4 nibble (v+8), even element low; q3 field (v+4) at bits
+//          3*(e%8) of the little-endian 3-byte granule e/8.
+// Eight threads own one group (eight consecutive elements each, two 16-byte
+// loads), reduce amax with three shuffles and write one packed word each.
+#pragma once
+
+#include "common.cuh"
+
+namespace va {
+
+__device__ __forceinline__ int lrint_narrow(float y) {
+    if (!(fabsf(y) < 9.2233720368547758e18f)) return 0;  // nan, +-inf, |y| >= 2^63
+    const long long t = __float2ll_rn(y);                 // round half to even
+    return (int)(unsigned int)(unsigned long long)t;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
+                                                       __half* __restrict__ scales, long long ngroups) {
+    constexpr int lim = BITS == 8 ? 127 : BITS == 4 ? 7 : 3;
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long grp = tid >> 3;
+    const int part = (int)(tid & 7);
+    const bool active = grp < ngroups;
+    float v[8];
+    if (active) {
+        const float4* p = reinterpret_cast<const float4*>(x + grp * kGroup + part * 8);
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));  // fmaxf drops nan operands
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (!active) return;
+
+    const float s = amax > 0.f ? __fdiv_rn(amax, (float)lim) : 1.f;
+    const __half hs = __float2half_rn(s);
+    const float sh = __half2float(hs);
+    int c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = max(-lim, min(lim, lrint_narrow(__fdiv_rn(v[i], sh))));
+
+    const long long e0 = grp * kGroup + part * 8;  // first element of this thread
+    if constexpr (BITS == 8) {
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0 |= (uint32_t)(uint8_t)(int8_t)c[i] << (8 * i);
+            w1 |= (uint32_t)(uint8_t)(int8_t)c[4 + i] << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(codes + e0) = make_uint2(w0, w1);
+    } else if constexpr (BITS == 4) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w |= (uint32_t)(c[i] + 8) << (4 * i);
+        *reinterpret_cast<uint32_t*>(codes + e0 / 2) = w;
+    } else {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w |= (uint32_t)(c[i] + 4) << (3 * i);
+        uint8_t* dst = codes + (e0 / 8) * 3;
+        dst[0] = (uint8_t)w;
+        dst[1] = (uint8_t)(w >> 8);
+        dst[2] = (uint8_t)(w >> 16);
+    }
+    if (part == 0) scales[grp] = hs;
+}
+
+}  // namespace va

@@ -1,0 +1,436 @@
+// C ABI of voltattn_b200 (declared in include/voltattn.h): argument checks,
+// workspace layout, kernel selection and launch. No CPU compute path: every
+// entry point either launches its kernels or returns an error status.
+
+#include <algorithm>
+#include <climits>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/voltattn.h"
+#include "common.cuh"
+#include "decode_plain.cuh"
+#include "decode_stream.cuh"
+#include "gqa.cuh"
+#include "probe.cuh"
+#include "quantize.cuh"
+
+using namespace va;
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+    t_last_cuda_error = (int)e;
+    return VA_ERR_CUDA;
+}
+
+#define VA_CUDA(call)                                   \
+    do {                                                \
+        const cudaError_t e__ = (call);                 \
+        if (e__ != cudaSuccess) return cuda_fail(e__);  \
+    } while (0)
+
+bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_Q3P; }
+bool is_f16(int f) { return f == VA_F16 || f == VA_F16P; }
+bool is_plain(int f) { return f == VA_F16 || f == VA_Q8 || f == VA_Q4; }
+int fmt_bits(int f) { return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P) ? 8 : (f == VA_Q3P) ? 3 : 4; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t slots_bytes(int H, int D, int S) { return (size_t)H * S * (D + 2) * sizeof(float); }
+size_t counters_offset(int H, int D, int S) { return (slots_bytes(H, D, S) + 255) & ~(size_t)255; }
+
+constexpr int kMaxDevices = 64;
+
+int current_device(int* dev) {
+    VA_CUDA(cudaGetDevice(dev));
+    if (*dev < 0 || *dev >= kMaxDevices) return VA_ERR_UNSUPPORTED;
+    return VA_OK;
+}
+
+int sm_count(int dev) {
+    static int cache[kMaxDevices] = {0};
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// Per (kernel configuration, device): dynamic smem attribute set and the
+// number of resident CTAs per SM.
+template <class C>
+int stream_ctas_per_sm(int dev, int* out) {
+    static int occ[kMaxDevices] = {0};
+    static std::mutex mu;
+    if (occ[dev] == 0) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ[dev] == 0) {
+            VA_CUDA(cudaFuncSetAttribute(decode_stream_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            int n = 0;
+            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_stream_kernel<C>, C::kThreads,
+                                                                  C::kSmemBytes));
+            occ[dev] = std::max(1, n);
+        }
+    }
+    *out = occ[dev];
+    return VA_OK;
+}
+
+template <class C>
+int launch_stream(const DecodeParams& p, cudaStream_t st) {
+    int dev, occ;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    rc = stream_ctas_per_sm<C>(dev, &occ);
+    if (rc) return rc;
+    const long long units = (long long)p.H * p.S;
+    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
+    decode_stream_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+template <Kind K>
+int launch_stream_d(const DecodeParams& p, int D, cudaStream_t st) {
+    return D == 128 ? launch_stream<StreamCfg<K, 128>>(p, st) : launch_stream<StreamCfg<K, 64>>(p, st);
+}
+
+int launch_stream_fmt(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
+    switch (fmt) {
+        case VA_F16P: return launch_stream_d<Kind::F16>(p, D, st);
+        case VA_Q8P: return launch_stream_d<Kind::Q8>(p, D, st);
+        case VA_Q4P: return launch_stream_d<Kind::Q4>(p, D, st);
+        case VA_Q3P: return launch_stream_d<Kind::Q3>(p, D, st);
+        default: return VA_ERR_INVALID;
+    }
+}
+
+template <int BITS>
+void launch_plain_bits(const va_bufs* b, float* ws, int H, int L, int D, int S, cudaStream_t st) {
+    const int chunk = (L + S - 1) / S;  // the reference's split rule, src/voltattn.cu:804
+    const dim3 grid((unsigned)H, (unsigned)S);
+    const auto* K = static_cast<const uint8_t*>(b->K);
+    const auto* V = static_cast<const uint8_t*>(b->V);
+    const auto* sK = static_cast<const __half*>(b->scK);
+    const auto* sV = static_cast<const __half*>(b->scV);
+    const auto* q = static_cast<const __half*>(b->q);
+    if (D == 128)
+        decode_plain_kernel<BITS, 128><<<grid, 32 * kPlainWarps, 0, st>>>(K, V, sK, sV, q, ws, L, S, chunk);
+    else
+        decode_plain_kernel<BITS, 64><<<grid, 32 * kPlainWarps, 0, st>>>(K, V, sK, sV, q, ws, L, S, chunk);
+}
+
+int check_decode_args(int fmt, const va_bufs* b, int H, int L, int D, int S) {
+    if (!is_valid_fmt(fmt) || !b) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (H < 1 || L < 1 || S < 1 || S > 65535) return VA_ERR_INVALID;
+    if ((long long)H * S > INT_MAX / 2) return VA_ERR_INVALID;
+    if (!b->K || !b->V || !b->q || !b->out) return VA_ERR_INVALID;
+    if (!is_f16(fmt) && (!b->scK || !b->scV)) return VA_ERR_INVALID;
+    if (!aligned16(b->K) || !aligned16(b->V)) return VA_ERR_ALIGN;
+    if (!is_f16(fmt) && (!aligned16(b->scK) || !aligned16(b->scV))) return VA_ERR_ALIGN;
+    if ((reinterpret_cast<uintptr_t>(b->q) & 1u) || (reinterpret_cast<uintptr_t>(b->out) & 1u)) return VA_ERR_ALIGN;
+    return VA_OK;
+}
+
+DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsigned* counters, int mode,
+                         float* partial) {
+    DecodeParams p;
+    p.K = static_cast<const uint8_t*>(b->K);
+    p.V = static_cast<const uint8_t*>(b->V);
+    p.scK = static_cast<const __half*>(b->scK);
+    p.scV = static_cast<const __half*>(b->scV);
+    p.q = static_cast<const __half*>(b->q);
+    p.out = static_cast<__half*>(b->out);
+    p.partial = partial;
+    p.ws = ws;
+    p.counters = counters;
+    p.H = H;
+    p.L = L;
+    p.S = S;
+    const int per = (L + S - 1) / S;
+    p.chunk = (per + 7) & ~7;  // whole 8-row blocks per split
+    p.total_rows = (long long)H * L;
+    p.out_mode = mode;
+    return p;
+}
+
+int stream_cfg_tile_rows(int fmt, int D) {
+    switch (fmt) {
+        case VA_F16P: return D == 128 ? StreamCfg<Kind::F16, 128>::kTr : StreamCfg<Kind::F16, 64>::kTr;
+        case VA_Q8P: return D == 128 ? StreamCfg<Kind::Q8, 128>::kTr : StreamCfg<Kind::Q8, 64>::kTr;
+        case VA_Q4P: return D == 128 ? StreamCfg<Kind::Q4, 128>::kTr : StreamCfg<Kind::Q4, 64>::kTr;
+        default: return D == 128 ? StreamCfg<Kind::Q3, 128>::kTr : StreamCfg<Kind::Q3, 64>::kTr;
+    }
+}
+
+int stream_cfg_occupancy(int fmt, int D, int dev, int* occ) {
+    switch (fmt) {
+        case VA_F16P:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::F16, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::F16, 64>>(dev, occ);
+        case VA_Q8P:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q8, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::Q8, 64>>(dev, occ);
+        case VA_Q4P:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q4, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::Q4, 64>>(dev, occ);
+        default:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q3, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::Q3, 64>>(dev, occ);
+    }
+}
+
+int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws, size_t ws_bytes, float* partial,
+                void* stream) {
+    int rc = check_decode_args(fmt, b, H, L, D, S);
+    if (rc) return rc;
+    if (!ws || !aligned16(ws) || ws_bytes < slots_bytes(H, D, S)) return VA_ERR_WORKSPACE;
+    const bool fused_ok = ws_bytes >= va_workspace_bytes(H, D, S);
+    if (partial && !fused_ok) return VA_ERR_WORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* slots = static_cast<float*>(ws);
+    if (is_plain(fmt) || !fused_ok) {
+        if (is_plain(fmt)) {
+            if (partial) return VA_ERR_UNSUPPORTED;
+            const int bits = fmt_bits(fmt);
+            if (bits == 16) launch_plain_bits<16>(b, slots, H, L, D, S, st);
+            else if (bits == 8) launch_plain_bits<8>(b, slots, H, L, D, S, st);
+            else launch_plain_bits<4>(b, slots, H, L, D, S, st);
+            VA_CUDA(cudaGetLastError());
+        } else {
+            const DecodeParams p = make_params(b, H, L, S, slots, nullptr, kOutSlots, nullptr);
+            rc = launch_stream_fmt(fmt, p, D, st);
+            if (rc) return rc;
+        }
+        combine_kernel<<<H, 128, 0, st>>>(slots, 1, H, S, D, static_cast<__half*>(b->out), nullptr, 0);
+        VA_CUDA(cudaGetLastError());
+        return VA_OK;
+    }
+    unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
+    const DecodeParams p =
+        make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+    return launch_stream_fmt(fmt, p, D, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int va_version(void) { return 100; }
+
+const char* va_fmt_name(int fmt) {
+    static const char* names[] = {"f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+"};
+    return is_valid_fmt(fmt) ? names[fmt] : nullptr;
+}
+
+int va_fmt_from_name(const char* name) {
+    if (!name) return -1;
+    for (int f = VA_F16; f <= VA_Q3P; ++f)
+        if (std::strcmp(name, va_fmt_name(f)) == 0) return f;
+    return -1;
+}
+
+int va_fmt_bits(int fmt) { return is_valid_fmt(fmt) ? fmt_bits(fmt) : -1; }
+
+size_t va_payload_bytes(int fmt, size_t n) {
+    if (!is_valid_fmt(fmt)) return 0;
+    const int bits = fmt_bits(fmt);
+    return bits == 16 ? 2 * n : bits == 8 ? n : bits == 4 ? n / 2 : n * 3 / 8;
+}
+
+const char* va_status_string(int status) {
+    switch (status) {
+        case VA_OK: return "ok";
+        case VA_ERR_INVALID: return "invalid argument (format, shape or null pointer)";
+        case VA_ERR_ALIGN: return "misaligned pointer (K/V/scales must be 16-byte aligned)";
+        case VA_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+        case VA_ERR_CUDA: return "CUDA runtime error (see va_last_cuda_error)";
+        case VA_ERR_UNSUPPORTED: return "unsupported configuration (D must be 64 or 128)";
+        case VA_ERR_DEVICE: return "a kernel reported a device-side error";
+        case VA_ERR_TOO_LARGE: return "size beyond the stated maximum";
+        default: return "unknown status";
+    }
+}
+
+int va_last_cuda_error(void) { return t_last_cuda_error; }
+
+size_t va_workspace_bytes(int H, int D, int S) {
+    if (H < 1 || S < 1 || D < 1) return 0;
+    return counters_offset(H, D, S) + (((size_t)H * sizeof(unsigned) + 255) & ~(size_t)255);
+}
+
+int va_workspace_init(void* ws, size_t bytes, void* stream) {
+    if (!ws) return VA_ERR_WORKSPACE;
+    VA_CUDA(cudaMemsetAsync(ws, 0, bytes, static_cast<cudaStream_t>(stream)));
+    return VA_OK;
+}
+
+int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
+    if (!S || !is_valid_fmt(fmt) || H < 1 || L < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    int dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const int nsm = sm_count(dev);
+    if (is_plain(fmt)) {
+        // one CTA per (head, split): aim for ~4 waves of 4-warp blocks
+        const int want = std::max(1, (nsm * 16) / H);
+        *S = std::max(1, std::min({want, (L + 63) / 64, 65535}));
+        return VA_OK;
+    }
+    int occ = 1;
+    rc = stream_cfg_occupancy(fmt, D, dev, &occ);
+    if (rc) return rc;
+    const long long cap = (long long)nsm * occ;
+    const int tr = stream_cfg_tile_rows(fmt, D);
+    // cost ~ (units per CTA) * (rows per unit + a fixed per-unit overhead of
+    // a quarter tile); keep units at least one 8-row block long
+    double best = 1e300;
+    int bestS = 1;
+    const int smax = std::min(65535, std::max(1, (L + 7) / 8));
+    for (int s = 1; s <= smax; ++s) {
+        const long long units = (long long)H * s;
+        const long long per_cta = (units + cap - 1) / cap;
+        const int rows = (((L + s - 1) / s) + 7) & ~7;
+        const double cost = (double)per_cta * (rows + 0.25 * tr);
+        if (cost < best - 1e-9) {
+            best = cost;
+            bestS = s;
+        }
+    }
+    *S = bestS;
+    return VA_OK;
+}
+
+int va_decode(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes, void* stream) {
+    return decode_impl(fmt, bufs, H, L, D, S, ws, ws_bytes, nullptr, stream);
+}
+
+int va_decode_partial(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes,
+                      float* partial, void* stream) {
+    if (!partial) return VA_ERR_INVALID;
+    if (is_plain(fmt)) return VA_ERR_UNSUPPORTED;
+    return decode_impl(fmt, bufs, H, L, D, S, ws, ws_bytes, partial, stream);
+}
+
+int va_combine_partials(const float* slots, int R, int H, int S, int D, void* out, void* stream) {
+    if (!slots || !out || R < 1 || H < 1 || S < 1 || D < 1 || D > 128) return VA_ERR_INVALID;
+    combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(slots, R, H, S, D,
+                                                                      static_cast<__half*>(out), nullptr, 0);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {
+    if (bits != 8 && bits != 4 && bits != 3) return VA_ERR_INVALID;
+    if (!x || !codes || !scales || H < 1 || L < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || !aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 1u)) return VA_ERR_ALIGN;
+    const long long ngroups = (long long)H * L * (D / kGroup);
+    const long long threads = ngroups * 8;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* c = static_cast<uint8_t*>(codes);
+    auto* s = static_cast<__half*>(scales);
+    if (bits == 8) quantize_kernel<8><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
+    else if (bits == 4) quantize_kernel<4><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
+    else quantize_kernel<3><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+int va_probe_ceiling_method(int device, int method, size_t bytes, int reps, double* gbs) {
+    if (!gbs || (method != 0 && method != 1)) return VA_ERR_INVALID;
+    if (bytes == 0) bytes = 4ull << 30;
+    if (reps <= 0) reps = 20;
+    bytes &= ~(size_t)(kProbeChunk - 1);
+    if (bytes < (size_t)kProbeChunk) return VA_ERR_INVALID;
+    int prev = 0;
+    VA_CUDA(cudaGetDevice(&prev));
+    VA_CUDA(cudaSetDevice(device));
+    if (device < 0 || device >= kMaxDevices) return VA_ERR_UNSUPPORTED;
+    void* buf = nullptr;
+    unsigned* sink = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = VA_OK;
+    do {
+        cudaError_t e = cudaMalloc(&buf, bytes);
+        if (e != cudaSuccess) { rc = cuda_fail(e); break; }
+        if ((e = cudaMalloc(&sink, 16)) != cudaSuccess) { rc = cuda_fail(e); break; }
+        if ((e = cudaMemset(buf, 0, bytes)) != cudaSuccess) { rc = cuda_fail(e); break; }
+        if ((e = cudaMemset(sink, 0, 16)) != cudaSuccess) { rc = cuda_fail(e); break; }
+        if ((e = cudaEventCreate(&e0)) != cudaSuccess || (e = cudaEventCreate(&e1)) != cudaSuccess) {
+            rc = cuda_fail(e);
+            break;
+        }
+        const int nsm = sm_count(device);
+        const int bulk_smem = kProbeStages * kProbeChunk + kProbeStages * 8;
+        if (method == 1) {
+            e = cudaFuncSetAttribute(probe_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bulk_smem);
+            if (e != cudaSuccess) { rc = cuda_fail(e); break; }
+        }
+        auto run = [&]() {
+            if (method == 0)
+                probe_vec_kernel<<<nsm * 4, 512>>>(static_cast<const uint4*>(buf), bytes / 16, sink);
+            else
+                probe_bulk_kernel<<<nsm, 32, bulk_smem>>>(static_cast<const uint8_t*>(buf), bytes / kProbeChunk,
+                                                          sink);
+        };
+        for (int w = 0; w < 3; ++w) run();
+        if ((e = cudaDeviceSynchronize()) != cudaSuccess) { rc = cuda_fail(e); break; }
+        double best = 0.0;
+        for (int r = 0; r < reps; ++r) {
+            cudaEventRecord(e0);
+            run();
+            cudaEventRecord(e1);
+            if ((e = cudaEventSynchronize(e1)) != cudaSuccess) { rc = cuda_fail(e); break; }
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, e0, e1);
+            if (ms > 0.f) best = std::max(best, (double)bytes / (ms * 1e6));
+        }
+        if (rc) break;
+        if ((e = cudaGetLastError()) != cudaSuccess) { rc = cuda_fail(e); break; }
+        *gbs = best;
+    } while (false);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (sink) cudaFree(sink);
+    if (buf) cudaFree(buf);
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int va_probe_ceiling(int device, size_t bytes, int reps, double* gbs) {
+    if (!gbs) return VA_ERR_INVALID;
+    double a = 0.0, b = 0.0;
+    int rc = va_probe_ceiling_method(device, 0, bytes, reps, &a);
+    if (rc) return rc;
+    rc = va_probe_ceiling_method(device, 1, bytes, reps, &b);
+    if (rc) return rc;
+    *gbs = std::max(a, b);
+    return VA_OK;
+}
+
+size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S) { return gqa_workspace_bytes(B, Hq, D, S); }
+
+int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax, int D, int S,
+                  void* ws, size_t ws_bytes, void* stream) {
+    return gqa_decode(fmt, bufs, lens, B, Hq, Hkv, Lmax, D, S, ws, ws_bytes, stream);
+}
+
+int va_device_error(int* code) {
+    if (!code) return VA_ERR_INVALID;
+    int v = 0;
+    VA_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+    const int zero = 0;
+    VA_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+    *code = v;
+    return VA_OK;
+}
+
+}  // extern "C"
