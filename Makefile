@@ -9,7 +9,7 @@ HDRS      := $(wildcard $(CSRC)/*.cuh) include/voltattn.h include/voltattn.hpp
 LIB       := voltattn_b200/libvoltattn_b200.so
 CLI       := voltattn_b200/bin/voltattn
 
-all: $(LIB) oracle
+all: $(LIB) $(CLI) oracle
 
 $(LIB): $(CSRC)/voltattn_api.cu $(HDRS)
 	$(NVCC) $(NVFLAGS) -shared -o $@ $(CSRC)/voltattn_api.cu 2> voltattn_b200/ptxas.log || (cat voltattn_b200/ptxas.log; false)

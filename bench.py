@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+",
                     help="formats also timed for the per-format table (empty: none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
     return ap.parse_args()
 
 
@@ -423,8 +425,31 @@ def run_ours(args, rank, world):
         dist.destroy_process_group()
 
 
+def run_profile(args):
+    """Small fixed workload for ncu captures: W warm-up then K decodes of one
+    cache (size it above the 126 MB L2 with --L)."""
+    import torch
+    import voltattn_b200 as va
+    dev = torch.device("cuda", 0)
+    fmt, L = args.fmt, args.L
+    cache = make_cache(va, torch, fmt, L, 99, dev)
+    q = torch.randn(H * D, device=dev).half()
+    out = torch.empty(H * D, dtype=torch.float16, device=dev)
+    S = va.suggest_splits(fmt, H, L, D)
+    ws = va.new_workspace(H, D, S, dev)
+    b = va.DeviceBufs(*cache, q, out, ws)
+    for _ in range(args.warmup + args.steps):
+        va.launch(fmt, b, H, L, D, S)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": fmt, "L": L, "splits": S, "launches": args.warmup + args.steps,
+                      "device_error": va.device_error()}))
+
+
 def main():
     args = parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
