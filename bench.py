@@ -241,7 +241,7 @@ def make_cache(va, torch, fmt, L, seed, dev):
     return K, V, sK, sV
 
 
-def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3):
+def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, splits=None):
     """Returns (ms_per_step, S, copies, launches_per_step) for K_steps decodes."""
     nbytes = algorithmic_bytes(fmt, L)
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
@@ -250,7 +250,7 @@ def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3):
     caches = [base] + [tuple(None if t is None else t.clone() for t in base) for _ in range(copies - 1)]
     q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 1)).half()
     out = torch.empty(H * D, dtype=torch.float16, device=dev)
-    S = va.suggest_splits(fmt, H, L, D)
+    S = splits or va.suggest_splits(fmt, H, L, D)
     ws = va.new_workspace(H, D, S, dev)
     bufs = [va.DeviceBufs(*c, q, out, ws) for c in caches]
     stream = torch.cuda.Stream(device=dev)

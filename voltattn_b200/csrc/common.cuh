@@ -107,6 +107,21 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Ticket for "the last one finishes the job": a gpu-scope acquire-release
+// add by one thread. Callers bracket it with a CTA barrier: the barrier orders
+// the other threads' slot writes before the release (cumulativity), and the
+// acquire orders the readers after the next barrier behind every earlier
+// release on the same counter. One thread fences instead of all of them.
+__device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void store_relaxed_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.gpu.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---- misc -----------------------------------------------------------------
 
 __device__ __forceinline__ float fast_exp2(float x) {

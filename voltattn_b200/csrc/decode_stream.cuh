@@ -2,26 +2,39 @@
 //
 // Same math as the reference's sub-warp kernels (src/voltattn.cu:364-649):
 // per head, score_j = q.K_j/sqrt(D), online softmax, o = sum_j p_j V_j, with
-// K/V dequantized in registers and fp32 accumulation. The B200 structure is
-// new:
-//   * persistent CTAs walk work units (head, split) = (h, s); a producer warp
-//     streams each unit's rows as tiles of TR rows through a STAGES-deep ring
-//     of shared-memory buffers with bulk asynchronous copies (cp.async.bulk,
-//     no multicast) completing on mbarriers, so tens of KB per SM are in
-//     flight without holding registers;
-//   * tiles start on global row multiples of 8, which makes every copy of
+// K/V dequantized in registers. The B200 structure is new:
+//
+//   * Persistent CTAs (two per SM) walk work units (head, split) = (h, s). A
+//     producer warp streams each unit's rows as tiles of TR rows (~32 KB of
+//     codes + scales) through a 3-deep ring of shared-memory stages with bulk
+//     asynchronous copies (cp.async.bulk, no multicast) completing on
+//     mbarriers. Copies are kept at 16 KB or more: small bulk copies (~4 KB)
+//     were measured to cap the per-SM stream rate far below HBM bandwidth.
+//   * The 8 consumer warps split each tile; a warp runs 32/LPR independent
+//     online-softmax chains (LPR lanes per row, 16 dims per lane; 8 for f16),
+//     each chain taking RPS rows of the tile with one max/rescale per batch.
+//   * Quantized K.q runs on the integer dot-product unit: q is held as 16-bit
+//     fixed point split into signed-high / unsigned-low byte planes, and each
+//     4-code word of K meets both planes in one dp4a each: exact integer
+//     arithmetic, no code is converted to float. (q4: nibbles are masked into
+//     even/odd byte lanes with the q planes permuted to match and the +8
+//     offset removed with a precomputed sum; q3: 3-bit fields are spread into
+//     byte lanes with masks and shifts, offset +4.)
+//   * Quantized p.V: the batch's weights e_j * vs_j become 16-bit fixed point
+//     relative to the batch maximum; the codes of 4 rows are byte-transposed
+//     (8 prmt per 4 words) so that one dp4a accumulates 4 rows of one dim;
+//     the integer sums are converted and folded into the fp32 output once
+//     per batch. Weight error <= 2^-16 of the batch maximum.
+//   * Tiles start on global row multiples of 8, which makes every copy of
 //     codes and scales 16-byte aligned and a multiple of 16 bytes for all
-//     formats and D in {64,128}; rows of neighbouring units that a tile
-//     covers are read but masked; the last (<8) rows of the whole tensor,
-//     which a 16-byte copy could overrun, are fetched with plain loads;
-//   * 8 consumer warps split each tile; a warp runs 32/LPR independent
-//     softmax chains (LPR lanes per row), each chain takes RPS rows per tile
-//     with one max/rescale per batch;
-//   * the unit's chains merge in registers (shuffles) then shared memory into
+//     formats and D in {64,128}; neighbouring rows a tile covers are masked
+//     (weight 0, score -inf, even if they hold nan); the last (<8) rows of the
+//     tensor, which a 16-byte copy could overrun, come from plain loads.
+//   * A unit's chains merge in registers (shuffles) then shared memory into
 //     one (m, l, o[D]) workspace slot (layout of src/voltattn.cu:92-93); the
-//     last CTA to finish a head (atomic ticket, no waiting) merges the head's
-//     S slots and writes the fp16 output — the reference's separate combine
-//     launch (src/voltattn.cu:651-672) is fused away.
+//     last CTA to finish a head (one acquire-release ticket, no waiting)
+//     merges the head's S slots and writes the output: the reference's
+//     separate combine launch (src/voltattn.cu:651-672) is fused away.
 // Every spin wait is bounded (kWaitLimitNs); on expiry the kernel records a
 // device error and returns.
 #pragma once
@@ -47,8 +60,8 @@ struct DecodeParams {
     float* ws;
     unsigned* counters;
     int H, L, S;
-    int chunk;            // positions per split (multiple of 8)
-    long long total_rows; // H * L
+    int chunk;             // positions per split (multiple of 8)
+    long long total_rows;  // H * L
     int out_mode;
 };
 
@@ -57,11 +70,11 @@ struct StreamCfg {
     static constexpr Kind kKind = K;
     static constexpr int kD = D;
     static constexpr int kBits = KindTraits<K>::kBits;
-    static constexpr int kDpl = KindTraits<K>::kDpl;
-    static constexpr int kLpr = D / kDpl;           // lanes per row
-    static constexpr int kNsg = 32 / kLpr;          // chains (sub-groups) per warp
-    static constexpr int kRps = (K == Kind::F16) ? 2 : 4;  // rows per chain per tile
-    static constexpr int kWarps = 8;                // consumer warps
+    static constexpr int kDpl = (K == Kind::F16) ? 8 : 16;                  // dims per lane
+    static constexpr int kLpr = D / kDpl;                                  // lanes per row
+    static constexpr int kNsg = 32 / kLpr;                                 // chains per warp
+    static constexpr int kRps = (K == Kind::F16 || K == Kind::Q8) ? 4 : 8;  // rows per chain per tile
+    static constexpr int kWarps = 8;                                       // consumer warps
     static constexpr int kThreads = (kWarps + 1) * 32;
     static constexpr int kTr = kWarps * kNsg * kRps;  // rows per tile
     static constexpr int kRb = D * kBits / 8;         // code bytes per row
@@ -74,6 +87,7 @@ struct StreamCfg {
     static_assert(kTr % 8 == 0, "tiles must be whole 8-row blocks");
     static_assert((kTr * kRb) % 16 == 0 && (kTr * kSb) % 16 == 0, "16-byte stage sections");
     static_assert(kDpl <= kGroup, "a lane's dims must lie in one quant group");
+    static_assert(kRps % 4 == 0, "rows per chain come in groups of 4");
 };
 
 struct UnitGeom {
@@ -97,6 +111,111 @@ __device__ __forceinline__ UnitGeom unit_geom(const DecodeParams& p, int u) {
     return g;
 }
 
+// ---- integer helpers ----------------------------------------------------------
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {  // a signed, b unsigned
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // a unsigned, b signed
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 4x4 byte transpose: byte j of in[i] -> byte i of out[j].
+__device__ __forceinline__ void transpose4x4(const uint32_t a, const uint32_t b, const uint32_t c, const uint32_t d,
+                                             uint32_t* o) {
+    const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(a, b, 0x7362);
+    const uint32_t t2 = __byte_perm(c, d, 0x5140), t3 = __byte_perm(c, d, 0x7362);
+    o[0] = __byte_perm(t0, t2, 0x5410);
+    o[1] = __byte_perm(t0, t2, 0x7632);
+    o[2] = __byte_perm(t1, t3, 0x5410);
+    o[3] = __byte_perm(t1, t3, 0x7632);
+}
+
+// q3: fields at bits 0, 6, 12, 18 (3 bits each) -> byte lanes 0..3.
+__device__ __forceinline__ uint32_t spread_q3(uint32_t x) {
+    x &= 0x1C71C7u;
+    x = (x & 0x1C7u) | ((x & 0x1C7000u) << 4);        // -> bits 0, 6, 16, 22
+    return (x & 0x70007u) | ((x & 0x1C001C0u) << 2);  // -> bits 0, 8, 16, 24
+}
+
+// ---- integer lane words -------------------------------------------------------------
+// Integer kinds present each lane's 16 codes as 4 words of 4 byte lanes. The
+// dim held by byte lane j of word w (word_dim) is a fixed permutation per
+// kind; the q planes are built in the same order and V sums are scattered
+// back through it, so results come out in natural dim order.
+//   q8: word w = dims 4w..4w+3 (signed codes)
+//   q4: word 2i = dims {8i, 8i+2, 8i+4, 8i+6}, word 2i+1 = {8i+1, ..., 8i+7}
+//       (unsigned v+8)
+//   q3: word 2i = fields {0,2,4,6} of granule i, word 2i+1 = fields {1,3,5,7}
+//       (unsigned v+4)
+
+template <Kind K>
+struct IntWords {
+    uint32_t w[4];
+};
+
+template <Kind K>
+__device__ __forceinline__ void load_int_words(IntWords<K>& r, const uint8_t* p) {
+    if constexpr (K == Kind::Q8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        r.w[0] = v.x;
+        r.w[1] = v.y;
+        r.w[2] = v.z;
+        r.w[3] = v.w;
+    } else if constexpr (K == Kind::Q4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        r.w[0] = v.x & 0x0F0F0F0Fu;
+        r.w[1] = (v.x >> 4) & 0x0F0F0F0Fu;
+        r.w[2] = v.y & 0x0F0F0F0Fu;
+        r.w[3] = (v.y >> 4) & 0x0F0F0F0Fu;
+    } else {
+        const uint16_t* p16 = reinterpret_cast<const uint16_t*>(p);
+        const uint32_t a = p16[0], b = p16[1], c = p16[2];
+        const uint32_t g0 = __byte_perm(a, b, 0x5410);  // bytes 0..2 of the slice
+        const uint32_t g1 = __byte_perm(b, c, 0x0541);  // bytes 3..5
+        r.w[0] = spread_q3(g0);
+        r.w[1] = spread_q3(g0 >> 3);
+        r.w[2] = spread_q3(g1);
+        r.w[3] = spread_q3(g1 >> 3);
+    }
+}
+
+template <Kind K>
+__host__ __device__ constexpr int word_dim(int w, int j) {
+    return K == Kind::Q8 ? 4 * w + j : 8 * (w / 2) + 2 * j + (w % 2);
+}
+
+// ---- f16 lane (fp32 math) ------------------------------------------------------------
+
+struct F16Lane {
+    float v[8];
+};
+
+__device__ __forceinline__ void load_f16_lane(F16Lane& r, const uint8_t* p) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        r.v[2 * i] = f.x;
+        r.v[2 * i + 1] = f.y;
+    }
+}
+
 // ---- producer warp ----------------------------------------------------------
 
 template <class C>
@@ -114,8 +233,7 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
             const uint32_t ph = (uint32_t)(k / C::kStages) & 1u;
             if (!mbar_wait_bounded(&empty[stage], ph ^ 1u)) {
                 if (lane == 0) report_error(kErrEmptyWait);
-                // drain: wait (bounded) for copies this warp may still have in flight
-                for (int d = 1; d <= C::kStages && k - d >= 0; ++d) {
+                for (int d = 1; d <= C::kStages && k - d >= 0; ++d) {  // drain own copies
                     const int kk = k - d;
                     mbar_wait_bounded(&full[kk % C::kStages], (uint32_t)(kk / C::kStages) & 1u);
                 }
@@ -172,32 +290,119 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
     }
 }
 
-// ---- consumer warps ---------------------------------------------------------
+// ---- consumer: per-head query state ---------------------------------------------
+
+template <class C>
+struct QState {
+    float qf[C::kDpl];      // f16: q * log2(e)/sqrt(D)
+    uint32_t qh[4], ql[4];  // integer kinds: signed-high / unsigned-low byte planes, word order
+    int qbias;              // q4 / q3: code offset * sum of this lane's fixed-point q
+    float qscale;           // 2^-e * log2(e) / sqrt(D)
+};
+
+template <class C>
+__device__ __forceinline__ void load_q(QState<C>& qs, const __half* qh, int sl) {
+    constexpr int D = C::kD;
+    const float base = rsqrtf((float)D) * kLog2e;
+    float x[C::kDpl];
+#pragma unroll
+    for (int d = 0; d < C::kDpl; ++d) x[d] = __half2float(qh[sl * C::kDpl + d]);
+    if constexpr (C::kKind == Kind::F16) {
+#pragma unroll
+        for (int d = 0; d < C::kDpl; ++d) qs.qf[d] = x[d] * base;
+    } else {
+        // per-head 16-bit fixed point with |q| * 2^e < 2^14 over the whole head
+        float amax = 0.f;
+#pragma unroll
+        for (int d = 0; d < C::kDpl; ++d) amax = fmaxf(amax, fabsf(x[d]));
+#pragma unroll
+        for (int off = 1; off < C::kLpr; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        int e = 0;
+        if (amax > 0.f) {
+            int ex;
+            frexpf(amax, &ex);  // amax < 2^ex
+            e = 14 - ex;
+        }
+        int qi[16];
+        int sum = 0;
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+            qi[d] = __float2int_rn(ldexpf(x[d], e));
+            sum += qi[d];
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            uint32_t h = 0, l = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int v = qi[word_dim<C::kKind>(w, j)];
+                h |= (uint32_t)((v >> 8) & 0xFF) << (8 * j);
+                l |= (uint32_t)(v & 0xFF) << (8 * j);
+            }
+            qs.qh[w] = h;
+            qs.ql[w] = l;
+        }
+        qs.qbias = (C::kKind == Kind::Q4) ? 8 * sum : (C::kKind == Kind::Q3) ? 4 * sum : 0;
+        qs.qscale = ldexpf(base, -e);
+    }
+}
+
+// Dot of one lane slice with q (before the group scale), in log2 units.
+template <class C>
+__device__ __forceinline__ float lane_score(const QState<C>& qs, const uint8_t* kp) {
+    if constexpr (C::kKind == Kind::F16) {
+        F16Lane r;
+        load_f16_lane(r, kp);
+        float acc = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) acc = fmaf(qs.qf[d], r.v[d], acc);
+        return acc;
+    } else {
+        IntWords<C::kKind> r;
+        load_int_words<C::kKind>(r, kp);
+        int hi = 0, lo = 0;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if constexpr (C::kKind == Kind::Q8) {
+                hi = dp4a_ss(r.w[w], qs.qh[w], hi);
+                lo = dp4a_su(r.w[w], qs.ql[w], lo);
+            } else {
+                hi = dp4a_us(r.w[w], qs.qh[w], hi);
+                lo = dp4a_uu(r.w[w], qs.ql[w], lo);
+            }
+        }
+        const int x = hi * 256 + lo - qs.qbias;
+        return (float)x * qs.qscale;
+    }
+}
+
+// ---- consumer: one tile --------------------------------------------------------
 
 template <class C, bool kMasked>
 __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp, int sg, int sl, long long t0,
-                                             long long r0, long long r1, const float* qf, float& m, float& l,
+                                             long long r0, long long r1, const QState<C>& qs, float& m, float& l,
                                              float* o) {
+    constexpr int kG = C::kSb / 2;
+    constexpr int R = C::kRps;
     const uint8_t* sK = stage_base;
     const uint8_t* sV = sK + C::kTr * C::kRb;
     const __half* sSK = reinterpret_cast<const __half*>(sV + C::kTr * C::kRb);
-    const __half* sSV = sSK + C::kTr * (C::kSb / 2);
-    constexpr int kG = C::kSb / 2;
+    const __half* sSV = sSK + C::kTr * kG;
     const int g = (sl * C::kDpl) / kGroup;
 
-    float s[C::kRps];
-    bool valid[C::kRps];
+    // scores of this chain's R rows: tile rows (warp*R + i)*Nsg + sg, so at
+    // each step i the warp reads Nsg consecutive rows, lane-contiguous
+    float s[R];
+    bool valid[R];
 #pragma unroll
-    for (int i = 0; i < C::kRps; ++i) {
-        const int lr = (warp * C::kRps + i) * C::kNsg + sg;  // tile-local row
+    for (int i = 0; i < R; ++i) {
+        const int lr = (warp * R + i) * C::kNsg + sg;
         valid[i] = true;
         if constexpr (kMasked) {
             const long long r = t0 + lr;
             valid[i] = (r >= r0) && (r < r1);
         }
-        LaneRaw<C::kKind> kr;
-        load_lane<C::kKind>(kr, sK + (size_t)lr * C::kRb + sl * C::kBpl);
-        float acc = lane_dot<C::kKind>(kr, qf, 0.f);
+        float acc = lane_score<C>(qs, sK + (size_t)lr * C::kRb + sl * C::kBpl);
         if constexpr (C::kKind != Kind::F16) acc *= __half2float(sSK[lr * kG + g]);
 #pragma unroll
         for (int off = C::kLpr / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
@@ -205,28 +410,91 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
     }
     float mnew = m;
 #pragma unroll
-    for (int i = 0; i < C::kRps; ++i) mnew = fmaxf(mnew, s[i]);
+    for (int i = 0; i < R; ++i) mnew = fmaxf(mnew, s[i]);
     const float c = fast_exp2(m - mnew);
     m = mnew;
-    l *= c;
+    float e[R];
+    float esum = 0.f;
 #pragma unroll
-    for (int d = 0; d < C::kDpl; ++d) o[d] *= c;
+    for (int i = 0; i < R; ++i) {
+        e[i] = fast_exp2(s[i] - mnew);
+        esum += e[i];
+    }
+    l = l * c + esum;
+
+    if constexpr (C::kKind == Kind::F16) {
 #pragma unroll
-    for (int i = 0; i < C::kRps; ++i) {
-        const int lr = (warp * C::kRps + i) * C::kNsg + sg;
-        const float e = fast_exp2(s[i] - mnew);
-        l += e;
-        float w = e;
-        if constexpr (C::kKind != Kind::F16) w *= __half2float(sSV[lr * kG + g]);
-        LaneRaw<C::kKind> vr;
-        load_lane<C::kKind>(vr, sV + (size_t)lr * C::kRb + sl * C::kBpl);
-        if constexpr (kMasked) {
-            if (!valid[i]) {
-                w = 0.f;
-                zero_lane<C::kKind>(vr);
+        for (int d = 0; d < 8; ++d) o[d] *= c;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int lr = (warp * R + i) * C::kNsg + sg;
+            F16Lane r;
+            load_f16_lane(r, sV + (size_t)lr * C::kRb + sl * C::kBpl);
+            if constexpr (kMasked) {
+                if (!valid[i]) {
+#pragma unroll
+                    for (int d = 0; d < 8; ++d) r.v[d] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[d] = fmaf(e[i], r.v[d], o[d]);
+        }
+    } else {
+        // weights e_i * vs_i as 16-bit fixed point relative to the batch max
+        float w[R];
+        float wmax = 0.f;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int lr = (warp * R + i) * C::kNsg + sg;
+            w[i] = e[i] * __half2float(sSV[lr * kG + g]);
+            if constexpr (kMasked) w[i] = valid[i] ? w[i] : 0.f;
+            wmax = fmaxf(wmax, w[i]);
+        }
+        const float inv = wmax > 0.f ? 32767.f / wmax : 0.f;
+        int acc_h[16], acc_l[16];
+#pragma unroll
+        for (int d = 0; d < 16; ++d) acc_h[d] = acc_l[d] = 0;
+        int psum = 0;
+#pragma unroll
+        for (int g4 = 0; g4 < R / 4; ++g4) {
+            uint32_t ph = 0, pl = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int pi = __float2int_rn(w[4 * g4 + j] * inv);
+                psum += pi;
+                ph |= (uint32_t)(pi >> 8) << (8 * j);
+                pl |= (uint32_t)(pi & 0xFF) << (8 * j);
+            }
+            IntWords<C::kKind> rw[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int lr = (warp * R + 4 * g4 + j) * C::kNsg + sg;
+                load_int_words<C::kKind>(rw[j], sV + (size_t)lr * C::kRb + sl * C::kBpl);
+            }
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                uint32_t t[4];  // t[j]: byte lane j of word wi for rows 0..3
+                transpose4x4(rw[0].w[wi], rw[1].w[wi], rw[2].w[wi], rw[3].w[wi], t);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int d = word_dim<C::kKind>(wi, j);
+                    if constexpr (C::kKind == Kind::Q8) {
+                        acc_h[d] = dp4a_su(t[j], ph, acc_h[d]);
+                        acc_l[d] = dp4a_su(t[j], pl, acc_l[d]);
+                    } else {
+                        acc_h[d] = dp4a_uu(t[j], ph, acc_h[d]);
+                        acc_l[d] = dp4a_uu(t[j], pl, acc_l[d]);
+                    }
+                }
             }
         }
-        lane_axpy<C::kKind>(vr, w, o);
+        const int bias = (C::kKind == Kind::Q4) ? 8 * psum : (C::kKind == Kind::Q3) ? 4 * psum : 0;
+        const float wscale = wmax * (1.f / 32767.f);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+            const int x = acc_h[d] * 256 + acc_l[d] - bias;
+            o[d] = fmaf((float)x, wscale, o[d] * c);
+        }
     }
 }
 
@@ -276,18 +544,14 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
     constexpr int kConsumerThreads = C::kWarps * 32;
     const int sg = lane / C::kLpr, sl = lane % C::kLpr;
     const int nunits = p.H * p.S;
-    // q scaled by log2(e)/sqrt(D): scores come out in log2 units for exp2
-    const float qscale = rsqrtf((float)D) * kLog2e;
-    float qf[C::kDpl];
+    QState<C> qs;
     int cur_h = -1;
-    int k = 0;
+    int k = 0;  // CTA tile counter (the producer's sequence)
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
         bool failed = false;
         const UnitGeom g = unit_geom<C>(p, u);
         if (g.h != cur_h) {
-            const __half* qh = p.q + (size_t)g.h * D + sl * C::kDpl;
-#pragma unroll
-            for (int d = 0; d < C::kDpl; ++d) qf[d] = __half2float(qh[d]) * qscale;
+            load_q<C>(qs, p.q + (size_t)g.h * D, sl);
             cur_h = g.h;
         }
         float m = kNegMax, l = 0.f, o[C::kDpl];
@@ -308,16 +572,15 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
             const long long t0 = g.a0 + (long long)t * C::kTr;
             const uint8_t* base = smem + (size_t)stage * C::kStageBytes;
             if (t0 >= g.r0 && t0 + C::kTr <= g.r1)
-                consume_tile<C, false>(base, warp, sg, sl, t0, g.r0, g.r1, qf, m, l, o);
+                consume_tile<C, false>(base, warp, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
             else
-                consume_tile<C, true>(base, warp, sg, sl, t0, g.r0, g.r1, qf, m, l, o);
+                consume_tile<C, true>(base, warp, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
         }
-        // A warp that gave up keeps taking part in this unit's barriers (with
-        // whatever partial state it has) so the other warps never block; after
-        // the unit all warps see the shared flag and return together. The
-        // error is visible through va_device_error.
+        // A warp that gave up keeps taking part in this unit's barriers so the
+        // others never block; after the unit all warps see the shared flag and
+        // return together. The error is visible through va_device_error.
 
         merge_chains_in_warp<C>(m, l, o);
         if (lane < C::kLpr) {
@@ -349,13 +612,11 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
             }
         }
         if (p.out_mode != kOutSlots) {
-            __threadfence();
             named_barrier_sync(1, kConsumerThreads);
-            if (tid == 0) *shTicket = (int)atomicAdd(&p.counters[g.h], 1u);
+            if (tid == 0) *shTicket = (int)atomic_add_acq_rel_gpu(&p.counters[g.h], 1u);
             named_barrier_sync(1, kConsumerThreads);
             if (*shTicket == p.S - 1) {
                 // last split of head h to finish: merge its S slots
-                __threadfence();
                 const float* hs = p.ws + (size_t)g.h * p.S * (D + 2);
                 float ms = kNegMax;
                 for (int s = 0; s < p.S; ++s) ms = fmaxf(ms, __ldcg(hs + (size_t)s * (D + 2)));
@@ -378,7 +639,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
                         }
                     }
                 }
-                if (tid == 0) p.counters[g.h] = 0u;  // leave the workspace ready for the next call
+                if (tid == 0) store_relaxed_gpu(&p.counters[g.h], 0u);  // ready for the next call
             }
         }
         named_barrier_sync(1, kConsumerThreads);

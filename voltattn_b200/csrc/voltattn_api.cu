@@ -288,8 +288,9 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
     if (rc) return rc;
     const long long cap = (long long)nsm * occ;
     const int tr = stream_cfg_tile_rows(fmt, D);
-    // cost ~ (units per CTA) * (rows per unit + a fixed per-unit overhead of
-    // a quarter tile); keep units at least one 8-row block long
+    // cost ~ (units per CTA) * (rows per unit + a fixed per-unit overhead:
+    // the merge and ticket, worth ~256 rows of streaming); keep units at
+    // least one 8-row block long
     double best = 1e300;
     int bestS = 1;
     const int smax = std::min(65535, std::max(1, (L + 7) / 8));
@@ -297,7 +298,7 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
         const long long units = (long long)H * s;
         const long long per_cta = (units + cap - 1) / cap;
         const int rows = (((L + s - 1) / s) + 7) & ~7;
-        const double cost = (double)per_cta * (rows + 0.25 * tr);
+        const double cost = (double)per_cta * (rows + 256.0 + 0.5 * tr);
         if (cost < best - 1e-9) {
             best = cost;
             bestS = s;
