@@ -122,6 +122,15 @@ __device__ __forceinline__ void store_relaxed_gpu(unsigned* p, unsigned v) {
     asm volatile("st.relaxed.gpu.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Programmatic dependent launch. wait: block until the preceding grid in the
+// stream has completed and its memory is visible (returns at once when the
+// launch was not programmatic); launch_dependents: allow the next grid, if
+// launched programmatically, to start its prologue.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- misc -----------------------------------------------------------------
 
 __device__ __forceinline__ float fast_exp2(float x) {

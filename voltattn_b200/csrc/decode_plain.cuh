@@ -8,6 +8,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "lse_merge.cuh"
 
 namespace va {
 
@@ -140,31 +141,27 @@ __global__ void __launch_bounds__(32 * kPlainWarps) decode_plain_kernel(const ui
 
 // Log-sum-exp merge of R*S slots per head (combine, src/voltattn.cu:651-672):
 // slots [R][H][S][D+2] with m in natural-log units. mode 0: fp16 out[H][D];
-// mode 1: fp32 partial[H][D+2] (merged m, l, o).
-__global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ slots, int R, int H, int S, int D,
-                                                      __half* __restrict__ out, float* __restrict__ partial,
-                                                      int mode) {
-    const int h = blockIdx.x, t = threadIdx.x;
-    auto slot = [&](int r, int s) { return slots + (((size_t)r * H + h) * S + s) * (D + 2); };
-    float ms = kNegMax;
-    for (int r = 0; r < R; ++r)
-        for (int s = 0; s < S; ++s) ms = fmaxf(ms, slot(r, s)[0]);
-    float ls = 0.f, od = 0.f;
-    for (int r = 0; r < R; ++r) {
-        for (int s = 0; s < S; ++s) {
-            const float* sp = slot(r, s);
-            const float a = fast_exp2((sp[0] - ms) * kLog2e);
-            ls += sp[1] * a;
-            if (t < D) od += sp[2 + t] * a;
-        }
-    }
-    if (t < D) {
+// mode 1: fp32 partial[H][D+2] (merged m, l, o). One 256-thread block per head.
+constexpr int kCombineThreads = 256;
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ slots, int R, int H,
+                                                                  int S, int D, __half* __restrict__ out,
+                                                                  float* __restrict__ partial, int mode) {
+    __shared__ float sh_a[kCombineThreads], sh_red[64];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    auto slot = [&](int i) {
+        const int r = i / S, s = i - r * S;
+        return slots + (((size_t)r * H + h) * S + s) * (D + 2);
+    };
+    float ms, ls, od;
+    lse_merge(slot, R * S, D, tid, kCombineThreads, LseScratch{sh_a, sh_red}, [] { __syncthreads(); }, ms, ls, od);
+    if (tid < D) {
         if (mode == 0) {
-            out[(size_t)h * D + t] = __float2half_rn(od / ls);
+            out[(size_t)h * D + tid] = __float2half_rn(od / ls);
         } else {
             float* pp = partial + (size_t)h * (D + 2);
-            pp[2 + t] = od;
-            if (t == 0) {
+            pp[2 + tid] = od;
+            if (tid == 0) {
                 pp[0] = ms;
                 pp[1] = ls;
             }

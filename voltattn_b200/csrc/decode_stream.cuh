@@ -40,6 +40,7 @@
 #pragma once
 
 #include "formats.cuh"
+#include "lse_merge.cuh"
 
 namespace va {
 
@@ -88,6 +89,7 @@ struct StreamCfg {
     static_assert((kTr * kRb) % 16 == 0 && (kTr * kSb) % 16 == 0, "16-byte stage sections");
     static_assert(kDpl <= kGroup, "a lane's dims must lie in one quant group");
     static_assert(kRps % 4 == 0, "rows per chain come in groups of 4");
+    static_assert(kWarps * D >= kWarps * 32 + 64, "merge area doubles as the combine scratch");
 };
 
 struct UnitGeom {
@@ -150,6 +152,16 @@ __device__ __forceinline__ uint32_t spread_q3(uint32_t x) {
     x &= 0x1C71C7u;
     x = (x & 0x1C7u) | ((x & 0x1C7000u) << 4);        // -> bits 0, 6, 16, 22
     return (x & 0x70007u) | ((x & 0x1C001C0u) << 2);  // -> bits 0, 8, 16, 24
+}
+
+// Exact int <-> float conversions for |x| < 2^22 without the XU pipe: the
+// value rides in the mantissa of 1.5 * 2^23 (one integer add + one float
+// add), instead of I2F / F2I, which share the transcendental unit with exp2.
+__device__ __forceinline__ float small_int_to_float(int x) {
+    return __int_as_float(x + 0x4B400000) - 12582912.0f;
+}
+__device__ __forceinline__ int float_to_small_int_rn(float f) {  // round to nearest even
+    return __float_as_int(f + 12582912.0f) - 0x4B400000;
 }
 
 // ---- integer lane words -------------------------------------------------------------
@@ -372,7 +384,10 @@ __device__ __forceinline__ float lane_score(const QState<C>& qs, const uint8_t* 
             }
         }
         const int x = hi * 256 + lo - qs.qbias;
-        return (float)x * qs.qscale;
+        // |x| < 2^22 for q4 / q3 (|q| < 2^14, codes <= 15, 16 dims); q8 sums
+        // can reach 2^25 and use the hardware converter
+        if constexpr (C::kKind == Kind::Q8) return (float)x * qs.qscale;
+        else return small_int_to_float(x) * qs.qscale;
     }
 }
 
@@ -460,7 +475,7 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
             uint32_t ph = 0, pl = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int pi = __float2int_rn(w[4 * g4 + j] * inv);
+                const int pi = float_to_small_int_rn(w[4 * g4 + j] * inv);  // 0..32767
                 psum += pi;
                 ph |= (uint32_t)(pi >> 8) << (8 * j);
                 pl |= (uint32_t)(pi & 0xFF) << (8 * j);
@@ -493,7 +508,9 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
 #pragma unroll
         for (int d = 0; d < 16; ++d) {
             const int x = acc_h[d] * 256 + acc_l[d] - bias;
-            o[d] = fmaf((float)x, wscale, o[d] * c);
+            // q4 / q3: |x| <= 8 rows * 32767 * 15 < 2^22; q8: up to 2^24
+            const float xf = (C::kKind == Kind::Q8) ? (float)x : small_int_to_float(x);
+            o[d] = fmaf(xf, wscale, o[d] * c);
         }
     }
 }
@@ -535,6 +552,12 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
         fence_mbar_init();
     }
     __syncthreads();
+    // Everything above touches only shared memory. Nothing below reads or
+    // writes global memory before the preceding grid has fully completed, so
+    // results equal plain stream order; the early trigger lets the next
+    // decode's CTAs be resident and initialised as soon as ours exit.
+    grid_dependency_wait();
+    if (threadIdx.x == 0) grid_launch_dependents();
 
     if (warp == C::kWarps) {
         stream_producer<C>(p, smem, full, empty);
@@ -616,18 +639,14 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
             if (tid == 0) *shTicket = (int)atomic_add_acq_rel_gpu(&p.counters[g.h], 1u);
             named_barrier_sync(1, kConsumerThreads);
             if (*shTicket == p.S - 1) {
-                // last split of head h to finish: merge its S slots
+                // last split of head h to finish: merge its S slots (the
+                // merge area is free again after the ticket barrier)
                 const float* hs = p.ws + (size_t)g.h * p.S * (D + 2);
-                float ms = kNegMax;
-                for (int s = 0; s < p.S; ++s) ms = fmaxf(ms, __ldcg(hs + (size_t)s * (D + 2)));
+                float ms, ls, od;
+                lse_merge([&](int i) { return hs + (size_t)i * (D + 2); }, p.S, D, tid, kConsumerThreads,
+                          LseScratch{shO, shO + kConsumerThreads},
+                          [] { named_barrier_sync(1, kConsumerThreads); }, ms, ls, od);
                 if (tid < D) {
-                    float ls = 0.f, od = 0.f;
-                    for (int s = 0; s < p.S; ++s) {
-                        const float* sp = hs + (size_t)s * (D + 2);
-                        const float a = fast_exp2((__ldcg(sp) - ms) * kLog2e);
-                        ls += __ldcg(sp + 1) * a;
-                        od += __ldcg(sp + 2 + tid) * a;
-                    }
                     if (p.out_mode == kOutHalf) {
                         p.out[(size_t)g.h * D + tid] = __float2half_rn(od / ls);
                     } else {

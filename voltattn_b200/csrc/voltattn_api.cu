@@ -89,8 +89,20 @@ int launch_stream(const DecodeParams& p, cudaStream_t st) {
     if (rc) return rc;
     const long long units = (long long)p.H * p.S;
     const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
-    decode_stream_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
-    VA_CUDA(cudaGetLastError());
+    // Programmatic stream serialization: the kernel waits for the preceding
+    // grid before any global access (griddepcontrol.wait), so only its launch
+    // latency and shared-memory prologue overlap the predecessor's tail.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_stream_kernel<C>, p));
     return VA_OK;
 }
 
@@ -207,7 +219,7 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
             rc = launch_stream_fmt(fmt, p, D, st);
             if (rc) return rc;
         }
-        combine_kernel<<<H, 128, 0, st>>>(slots, 1, H, S, D, static_cast<__half*>(b->out), nullptr, 0);
+        combine_kernel<<<H, kCombineThreads, 0, st>>>(slots, 1, H, S, D, static_cast<__half*>(b->out), nullptr, 0);
         VA_CUDA(cudaGetLastError());
         return VA_OK;
     }
@@ -321,7 +333,7 @@ int va_decode_partial(int fmt, const va_bufs* bufs, int H, int L, int D, int S, 
 
 int va_combine_partials(const float* slots, int R, int H, int S, int D, void* out, void* stream) {
     if (!slots || !out || R < 1 || H < 1 || S < 1 || D < 1 || D > 128) return VA_ERR_INVALID;
-    combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(slots, R, H, S, D,
+    combine_kernel<<<H, kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(slots, R, H, S, D,
                                                                       static_cast<__half*>(out), nullptr, 0);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
