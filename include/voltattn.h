@@ -173,6 +173,24 @@ VA_API size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S);
 VA_API int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax,
                          int D, int S, void* ws, size_t ws_bytes, void* stream);
 
+/* va_decode for callers that cannot allocate device memory. No counterpart in
+ * the reference. Some hosts of this library cannot call cudaMalloc: code
+ * running inside a CUDA-graph-building framework that forbids allocation
+ * between captures, plugins whose host owns the whole memory pool, and
+ * callers that keep device memory fixed after start-up. This entry point takes
+ * the same inputs and outputs as va_decode but no workspace. The workspace is
+ * a fixed 4 MiB array built into the library: every GPU that loads the
+ * library holds it until the process exits. The required size is
+ * va_workspace_bytes(H, D, S); calls that need more than 4 MiB return
+ * VA_ERR_TOO_LARGE before launching anything. The first call on a device looks
+ * up the array's device address (once per device, with that device current),
+ * so make that first call before any stream capture begins. Every call
+ * shares the one array: each call clears its completion counters on `stream`
+ * first, and calls whose kernels overlap on the GPU (different streams, or
+ * different host threads) race on it and must be serialised by the caller.
+ * Allocates nothing (no cudaMalloc, no cudaFree). */
+VA_API int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* stream);
+
 /* Device-side error word (bounded waits that gave up, etc.). Reads and clears
  * the flag of the current device; *code = 0 when no kernel reported one. */
 VA_API int va_device_error(int* code);

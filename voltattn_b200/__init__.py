@@ -59,6 +59,7 @@ def _load():
     lib.va_gqa_workspace_bytes.argtypes = [i, i, i, i]; lib.va_gqa_workspace_bytes.restype = sz
     lib.va_decode_gqa.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_gqa.restype = i
+    lib.va_decode_noalloc.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, vp]; lib.va_decode_noalloc.restype = i
     lib.va_device_error.argtypes = [C.POINTER(i)]; lib.va_device_error.restype = i
     return lib
 

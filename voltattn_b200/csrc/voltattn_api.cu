@@ -229,6 +229,25 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
     return launch_stream_fmt(fmt, p, D, st);
 }
 
+// Fixed workspace of va_decode_noalloc (see include/voltattn.h). In host
+// code the symbol is only a handle: its device address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+int noalloc_scratch(int dev, void** out) {
+    static void* addr[kMaxDevices] = {nullptr};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        VA_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return VA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -434,6 +453,25 @@ size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S) { return gqa_workspac
 int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax, int D, int S,
                   void* ws, size_t ws_bytes, void* stream) {
     return gqa_decode(fmt, bufs, lens, B, Hq, Hkv, Lmax, D, S, ws, ws_bytes, stream);
+}
+
+int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* stream) {
+    const int rc = check_decode_args(fmt, bufs, H, L, D, S);
+    if (rc) return rc;
+    const size_t need = va_workspace_bytes(H, D, S);
+    if (need > kNoAllocScratchBytes) return VA_ERR_TOO_LARGE;
+    int dev;
+    int r = current_device(&dev);
+    if (r) return r;
+    void* ws = nullptr;
+    r = noalloc_scratch(dev, &ws);
+    if (r) return r;
+    // the array keeps the previous call's contents: zero the counters the
+    // fused combine expects, in stream order before the decode
+    unsigned char* base = static_cast<unsigned char*>(ws);
+    VA_CUDA(cudaMemsetAsync(base + counters_offset(H, D, S), 0, need - counters_offset(H, D, S),
+                            static_cast<cudaStream_t>(stream)));
+    return decode_impl(fmt, bufs, H, L, D, S, ws, need, nullptr, stream);
 }
 
 int va_device_error(int* code) {
