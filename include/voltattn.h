@@ -167,8 +167,11 @@ VA_API int va_probe_ceiling_method(int device, int method, size_t bytes, int rep
  * K/V: [B][Hkv][Lmax][D] rows in format fmt (rows >= lens[b] are never read),
  * scales [B][Hkv][Lmax][D/64]; q, out: __half [B][Hq][D]; lens: device int32
  * [B], 1 <= lens[b] <= Lmax. Query head hq reads KV head hq / (Hq / Hkv).
- * Each (sequence, KV head) streams its cache once for all of its query heads.
- * S = max splits per sequence; ws_bytes >= va_gqa_workspace_bytes(...). */
+ * Each (sequence, KV head) streams its cache once for all of its query heads
+ * (G = Hq/Hkv in {1, 2, 4, 8}; "+" formats only). S = splits per sequence:
+ * positions [s*c, (s+1)*c) with c = Lmax/S rounded up to 8 (splits past
+ * lens[b] are empty). ws_bytes >= va_gqa_workspace_bytes(B, Hq, D, S), zeroed
+ * before first use like va_decode's workspace. */
 VA_API size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S);
 VA_API int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax,
                          int D, int S, void* ws, size_t ws_bytes, void* stream);

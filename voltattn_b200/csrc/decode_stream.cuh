@@ -60,16 +60,21 @@ struct DecodeParams {
     float* partial;
     float* ws;
     unsigned* counters;
-    int H, L, S;
+    int H, L, S;           // H: KV streams (B * Hkv), L: rows per stream (Lmax)
     int chunk;             // positions per split (multiple of 8)
     long long total_rows;  // H * L
     int out_mode;
+    int Hkv;               // KV heads per sequence (== H for batch-1 decode)
+    const int* lens;       // per-sequence valid lengths (nullptr: all L)
 };
 
-template <Kind K, int D>
+// G = query heads per KV head (1: the reference's batch-1 multi-head decode;
+// 2/4/8: grouped-query decode, the G heads share every streamed tile).
+template <Kind K, int D, int G = 1>
 struct StreamCfg {
     static constexpr Kind kKind = K;
     static constexpr int kD = D;
+    static constexpr int kG = G;
     static constexpr int kBits = KindTraits<K>::kBits;
     static constexpr int kDpl = (K == Kind::F16) ? 8 : 16;                  // dims per lane
     static constexpr int kLpr = D / kDpl;                                  // lanes per row
@@ -78,6 +83,7 @@ struct StreamCfg {
     static constexpr int kWarps = 8;                                       // consumer warps
     static constexpr int kThreads = (kWarps + 1) * 32;
     static constexpr int kTr = kWarps * kNsg * kRps;  // rows per tile
+    static constexpr int kWpg = kWarps / G;           // warps per query head
     static constexpr int kRb = D * kBits / 8;         // code bytes per row
     static constexpr int kSb = (K == Kind::F16) ? 0 : 2 * (D / kGroup);  // scale bytes per row
     static constexpr int kBpl = kDpl * kBits / 8;     // code bytes per lane
@@ -89,11 +95,12 @@ struct StreamCfg {
     static_assert((kTr * kRb) % 16 == 0 && (kTr * kSb) % 16 == 0, "16-byte stage sections");
     static_assert(kDpl <= kGroup, "a lane's dims must lie in one quant group");
     static_assert(kRps % 4 == 0, "rows per chain come in groups of 4");
+    static_assert(G >= 1 && kWarps % G == 0, "query heads must divide the consumer warps");
     static_assert(kWarps * D >= kWarps * 32 + 64, "merge area doubles as the combine scratch");
 };
 
 struct UnitGeom {
-    int h, s;
+    int h, s;          // KV stream (sequence * Hkv + KV head), split
     long long r0, r1;  // unit's global rows [r0, r1)
     long long a0;      // first tile's first row (r0 rounded down to 8)
     int ntiles;
@@ -104,8 +111,9 @@ __device__ __forceinline__ UnitGeom unit_geom(const DecodeParams& p, int u) {
     UnitGeom g;
     g.h = u / p.S;
     g.s = u - g.h * p.S;
-    const long long j0 = min((long long)p.L, (long long)g.s * p.chunk);
-    const long long j1 = min((long long)p.L, j0 + p.chunk);
+    const long long len = p.lens ? (long long)min(max(__ldg(p.lens + g.h / p.Hkv), 0), p.L) : (long long)p.L;
+    const long long j0 = min(len, (long long)g.s * p.chunk);
+    const long long j1 = min(len, j0 + p.chunk);
     g.r0 = (long long)g.h * p.L + j0;
     g.r1 = (long long)g.h * p.L + j1;
     g.a0 = g.r0 & ~7ll;
@@ -394,7 +402,7 @@ __device__ __forceinline__ float lane_score(const QState<C>& qs, const uint8_t* 
 // ---- consumer: one tile --------------------------------------------------------
 
 template <class C, bool kMasked>
-__device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp, int sg, int sl, long long t0,
+__device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, int sg, int sl, long long t0,
                                              long long r0, long long r1, const QState<C>& qs, float& m, float& l,
                                              float* o) {
     constexpr int kG = C::kSb / 2;
@@ -405,13 +413,14 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
     const __half* sSV = sSK + C::kTr * kG;
     const int g = (sl * C::kDpl) / kGroup;
 
-    // scores of this chain's R rows: tile rows (warp*R + i)*Nsg + sg, so at
-    // each step i the warp reads Nsg consecutive rows, lane-contiguous
+    // scores of this chain's R rows: tile rows (rb*R + i)*Nsg + sg of row
+    // block rb, so at each step i the warp reads Nsg consecutive rows,
+    // lane-contiguous
     float s[R];
     bool valid[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-        const int lr = (warp * R + i) * C::kNsg + sg;
+        const int lr = (rb * R + i) * C::kNsg + sg;
         valid[i] = true;
         if constexpr (kMasked) {
             const long long r = t0 + lr;
@@ -442,7 +451,7 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
         for (int d = 0; d < 8; ++d) o[d] *= c;
 #pragma unroll
         for (int i = 0; i < R; ++i) {
-            const int lr = (warp * R + i) * C::kNsg + sg;
+            const int lr = (rb * R + i) * C::kNsg + sg;
             F16Lane r;
             load_f16_lane(r, sV + (size_t)lr * C::kRb + sl * C::kBpl);
             if constexpr (kMasked) {
@@ -460,7 +469,7 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
         float wmax = 0.f;
 #pragma unroll
         for (int i = 0; i < R; ++i) {
-            const int lr = (warp * R + i) * C::kNsg + sg;
+            const int lr = (rb * R + i) * C::kNsg + sg;
             w[i] = e[i] * __half2float(sSV[lr * kG + g]);
             if constexpr (kMasked) w[i] = valid[i] ? w[i] : 0.f;
             wmax = fmaxf(wmax, w[i]);
@@ -483,7 +492,7 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int warp
             IntWords<C::kKind> rw[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int lr = (warp * R + 4 * g4 + j) * C::kNsg + sg;
+                const int lr = (rb * R + 4 * g4 + j) * C::kNsg + sg;
                 load_int_words<C::kKind>(rw[j], sV + (size_t)lr * C::kRb + sl * C::kBpl);
             }
 #pragma unroll
@@ -566,6 +575,8 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
 
     constexpr int kConsumerThreads = C::kWarps * 32;
     const int sg = lane / C::kLpr, sl = lane % C::kLpr;
+    const int hk = warp / C::kWpg;   // this warp's query head within the group
+    const int wig = warp % C::kWpg;  // and its index among that head's warps
     const int nunits = p.H * p.S;
     QState<C> qs;
     int cur_h = -1;
@@ -574,7 +585,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
         bool failed = false;
         const UnitGeom g = unit_geom<C>(p, u);
         if (g.h != cur_h) {
-            load_q<C>(qs, p.q + (size_t)g.h * D, sl);
+            load_q<C>(qs, p.q + ((size_t)g.h * C::kG + hk) * D, sl);
             cur_h = g.h;
         }
         float m = kNegMax, l = 0.f, o[C::kDpl];
@@ -594,10 +605,16 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
             }
             const long long t0 = g.a0 + (long long)t * C::kTr;
             const uint8_t* base = smem + (size_t)stage * C::kStageBytes;
-            if (t0 >= g.r0 && t0 + C::kTr <= g.r1)
-                consume_tile<C, false>(base, warp, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
-            else
-                consume_tile<C, true>(base, warp, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
+            const bool interior = t0 >= g.r0 && t0 + C::kTr <= g.r1;
+            // the head's kWpg warps split the tile; each takes G row blocks
+#pragma unroll
+            for (int j = 0; j < C::kG; ++j) {
+                const int rb = wig * C::kG + j;
+                if (interior)
+                    consume_tile<C, false>(base, rb, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
+                else
+                    consume_tile<C, true>(base, rb, sg, sl, t0, g.r0, g.r1, qs, m, l, o);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
         }
@@ -616,22 +633,26 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
         }
         named_barrier_sync(1, kConsumerThreads);
         const int tid = threadIdx.x;
-        float* slot = p.ws + ((size_t)g.h * p.S + g.s) * (D + 2);
         if (tid < D) {
-            float ms = kNegMax;
 #pragma unroll
-            for (int w = 0; w < C::kWarps; ++w) ms = fmaxf(ms, shM[w]);
-            float ls = 0.f, od = 0.f;
+            for (int kq = 0; kq < C::kG; ++kq) {
+                const int w0 = kq * C::kWpg;
+                float ms = kNegMax;
 #pragma unroll
-            for (int w = 0; w < C::kWarps; ++w) {
-                const float a = fast_exp2(shM[w] - ms);
-                ls += shL[w] * a;
-                od += shO[w * D + tid] * a;
-            }
-            slot[2 + tid] = od;
-            if (tid == 0) {
-                slot[0] = ms * kLn2;  // natural-log units, as the reference's slots
-                slot[1] = ls;
+                for (int w = 0; w < C::kWpg; ++w) ms = fmaxf(ms, shM[w0 + w]);
+                float ls = 0.f, od = 0.f;
+#pragma unroll
+                for (int w = 0; w < C::kWpg; ++w) {
+                    const float a = fast_exp2(shM[w0 + w] - ms);
+                    ls += shL[w0 + w] * a;
+                    od += shO[(w0 + w) * D + tid] * a;
+                }
+                float* slot = p.ws + (((size_t)g.h * C::kG + kq) * p.S + g.s) * (D + 2);
+                slot[2 + tid] = od;
+                if (tid == 0) {
+                    slot[0] = ms * kLn2;  // natural-log units, as the reference's slots
+                    slot[1] = ls;
+                }
             }
         }
         if (p.out_mode != kOutSlots) {
@@ -639,22 +660,26 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
             if (tid == 0) *shTicket = (int)atomic_add_acq_rel_gpu(&p.counters[g.h], 1u);
             named_barrier_sync(1, kConsumerThreads);
             if (*shTicket == p.S - 1) {
-                // last split of head h to finish: merge its S slots (the
-                // merge area is free again after the ticket barrier)
-                const float* hs = p.ws + (size_t)g.h * p.S * (D + 2);
-                float ms, ls, od;
-                lse_merge([&](int i) { return hs + (size_t)i * (D + 2); }, p.S, D, tid, kConsumerThreads,
-                          LseScratch{shO, shO + kConsumerThreads},
-                          [] { named_barrier_sync(1, kConsumerThreads); }, ms, ls, od);
-                if (tid < D) {
-                    if (p.out_mode == kOutHalf) {
-                        p.out[(size_t)g.h * D + tid] = __float2half_rn(od / ls);
-                    } else {
-                        float* pp = p.partial + (size_t)g.h * (D + 2);
-                        pp[2 + tid] = od;
-                        if (tid == 0) {
-                            pp[0] = ms;
-                            pp[1] = ls;
+                // last split of this KV stream to finish: merge the S slots of
+                // each of its query heads (the merge area is free again after
+                // the ticket barrier)
+                for (int kq = 0; kq < C::kG; ++kq) {
+                    const size_t hq = (size_t)g.h * C::kG + kq;
+                    const float* hs = p.ws + hq * p.S * (D + 2);
+                    float ms, ls, od;
+                    lse_merge([&](int i) { return hs + (size_t)i * (D + 2); }, p.S, D, tid, kConsumerThreads,
+                              LseScratch{shO, shO + kConsumerThreads},
+                              [] { named_barrier_sync(1, kConsumerThreads); }, ms, ls, od);
+                    if (tid < D) {
+                        if (p.out_mode == kOutHalf) {
+                            p.out[hq * D + tid] = __float2half_rn(od / ls);
+                        } else {
+                            float* pp = p.partial + hq * (D + 2);
+                            pp[2 + tid] = od;
+                            if (tid == 0) {
+                                pp[0] = ms;
+                                pp[1] = ls;
+                            }
                         }
                     }
                 }

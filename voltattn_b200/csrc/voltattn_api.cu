@@ -11,7 +11,6 @@
 #include "common.cuh"
 #include "decode_plain.cuh"
 #include "decode_stream.cuh"
-#include "gqa.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
 
@@ -121,6 +120,27 @@ int launch_stream_fmt(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
     }
 }
 
+template <Kind K, int G>
+int launch_stream_dg(const DecodeParams& p, int D, cudaStream_t st) {
+    return D == 128 ? launch_stream<StreamCfg<K, 128, G>>(p, st) : launch_stream<StreamCfg<K, 64, G>>(p, st);
+}
+
+template <int G>
+int launch_stream_fmt_g(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
+    switch (fmt) {
+        case VA_F16P: return launch_stream_dg<Kind::F16, G>(p, D, st);
+        case VA_Q8P: return launch_stream_dg<Kind::Q8, G>(p, D, st);
+        case VA_Q4P: return launch_stream_dg<Kind::Q4, G>(p, D, st);
+        case VA_Q3P: return launch_stream_dg<Kind::Q3, G>(p, D, st);
+        default: return VA_ERR_UNSUPPORTED;
+    }
+}
+
+size_t gqa_ws_bytes(int B, int Hq, int Hkv, int D, int S) {
+    const size_t slots = (size_t)B * Hq * S * (D + 2) * sizeof(float);
+    return ((slots + 255) & ~(size_t)255) + (((size_t)B * Hkv * sizeof(unsigned) + 255) & ~(size_t)255);
+}
+
 template <int BITS>
 void launch_plain_bits(const va_bufs* b, float* ws, int H, int L, int D, int S, cudaStream_t st) {
     const int chunk = (L + S - 1) / S;  // the reference's split rule, src/voltattn.cu:804
@@ -168,6 +188,8 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.chunk = (per + 7) & ~7;  // whole 8-row blocks per split
     p.total_rows = (long long)H * L;
     p.out_mode = mode;
+    p.Hkv = H;
+    p.lens = nullptr;
     return p;
 }
 
@@ -448,11 +470,35 @@ int va_probe_ceiling(int device, size_t bytes, int reps, double* gbs) {
     return VA_OK;
 }
 
-size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S) { return gqa_workspace_bytes(B, Hq, D, S); }
+size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S) {
+    if (B < 1 || Hq < 1 || D < 1 || S < 1) return 0;
+    return gqa_ws_bytes(B, Hq, Hq, D, S);  // counters sized for the largest Hkv (= Hq)
+}
 
-int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax, int D, int S,
+int va_decode_gqa(int fmt, const va_bufs* b, const int* lens, int B, int Hq, int Hkv, int Lmax, int D, int S,
                   void* ws, size_t ws_bytes, void* stream) {
-    return gqa_decode(fmt, bufs, lens, B, Hq, Hkv, Lmax, D, S, ws, ws_bytes, stream);
+    if (!is_valid_fmt(fmt) || !b || !lens) return VA_ERR_INVALID;
+    if (is_plain(fmt)) return VA_ERR_UNSUPPORTED;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv) return VA_ERR_INVALID;
+    const int G = Hq / Hkv;
+    if (G != 1 && G != 2 && G != 4 && G != 8) return VA_ERR_UNSUPPORTED;
+    const long long streams = (long long)B * Hkv;
+    if (streams > INT_MAX / 2) return VA_ERR_INVALID;
+    int rc = check_decode_args(fmt, b, (int)streams, Lmax, D, S);
+    if (rc) return rc;
+    if (!ws || !aligned16(ws) || ws_bytes < gqa_ws_bytes(B, Hq, Hkv, D, S)) return VA_ERR_WORKSPACE;
+    const size_t slots = (size_t)B * Hq * S * (D + 2) * sizeof(float);
+    unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ((slots + 255) & ~(size_t)255));
+    DecodeParams p = make_params(b, (int)streams, Lmax, S, static_cast<float*>(ws), counters, kOutHalf, nullptr);
+    p.Hkv = Hkv;
+    p.lens = lens;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (G) {
+        case 1: return launch_stream_fmt_g<1>(fmt, p, D, st);
+        case 2: return launch_stream_fmt_g<2>(fmt, p, D, st);
+        case 4: return launch_stream_fmt_g<4>(fmt, p, D, st);
+        default: return launch_stream_fmt_g<8>(fmt, p, D, st);
+    }
 }
 
 int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* stream) {
