@@ -314,10 +314,10 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
 
 template <class C>
 struct QState {
-    float qf[C::kDpl];      // f16: q * log2(e)/sqrt(D)
-    uint32_t qh[4], ql[4];  // integer kinds: signed-high / unsigned-low byte planes, word order
-    int qbias;              // q4 / q3: code offset * sum of this lane's fixed-point q
-    float qscale;           // 2^-e * log2(e) / sqrt(D)
+    float qf[C::kDpl];  // f16: q * log2(e)/sqrt(D)
+    uint32_t qp[8];     // integer kinds: q as 16-bit pairs, qp[2w] = byte lanes 0,1 of word w, qp[2w+1] = 2,3
+    int qbias;          // q4 / q3: code offset * sum of this lane's fixed-point q
+    float qscale;       // 2^-e * log2(e) / sqrt(D)
 };
 
 template <class C>
@@ -352,19 +352,34 @@ __device__ __forceinline__ void load_q(QState<C>& qs, const __half* qh, int sl) 
         }
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            uint32_t h = 0, l = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int v = qi[word_dim<C::kKind>(w, j)];
-                h |= (uint32_t)((v >> 8) & 0xFF) << (8 * j);
-                l |= (uint32_t)(v & 0xFF) << (8 * j);
-            }
-            qs.qh[w] = h;
-            qs.ql[w] = l;
+            const auto pair = [&](int j) {
+                return ((uint32_t)qi[word_dim<C::kKind>(w, j)] & 0xFFFFu) |
+                       ((uint32_t)qi[word_dim<C::kKind>(w, j + 1)] << 16);
+            };
+            qs.qp[2 * w] = pair(0);
+            qs.qp[2 * w + 1] = pair(2);
         }
         qs.qbias = (C::kKind == Kind::Q4) ? 8 * sum : (C::kKind == Kind::Q3) ? 4 * sum : 0;
         qs.qscale = ldexpf(base, -e);
     }
+}
+
+// dp2a: c + a.h0 * b.b(0|2) + a.h1 * b.b(1|3); a = two 16-bit values, b = four bytes
+template <bool kHi, bool kASigned, bool kBSigned>
+__device__ __forceinline__ int dp2a(uint32_t a, uint32_t b, int c) {
+    int d;
+    if constexpr (kHi) {
+        if constexpr (kASigned && kBSigned) asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else if constexpr (kASigned) asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else if constexpr (kBSigned) asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else asm("dp2a.hi.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    } else {
+        if constexpr (kASigned && kBSigned) asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else if constexpr (kASigned) asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else if constexpr (kBSigned) asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+        else asm("dp2a.lo.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    }
+    return d;
 }
 
 // Dot of one lane slice with q (before the group scale), in log2 units.
@@ -380,20 +395,15 @@ __device__ __forceinline__ float lane_score(const QState<C>& qs, const uint8_t* 
     } else {
         IntWords<C::kKind> r;
         load_int_words<C::kKind>(r, kp);
-        int hi = 0, lo = 0;
+        constexpr bool kSignedCodes = C::kKind == Kind::Q8;
+        int x = -qs.qbias;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            if constexpr (C::kKind == Kind::Q8) {
-                hi = dp4a_ss(r.w[w], qs.qh[w], hi);
-                lo = dp4a_su(r.w[w], qs.ql[w], lo);
-            } else {
-                hi = dp4a_us(r.w[w], qs.qh[w], hi);
-                lo = dp4a_uu(r.w[w], qs.ql[w], lo);
-            }
+            x = dp2a<false, true, kSignedCodes>(qs.qp[2 * w], r.w[w], x);
+            x = dp2a<true, true, kSignedCodes>(qs.qp[2 * w + 1], r.w[w], x);
         }
-        const int x = hi * 256 + lo - qs.qbias;
-        // |x| < 2^22 for q4 / q3 (|q| < 2^14, codes <= 15, 16 dims); q8 sums
-        // can reach 2^25 and use the hardware converter
+        // |x| < 2^22 for q4 / q3 (|q| < 2^14, |v| <= 7, 16 dims); q8 sums can
+        // reach 2^25 and use the hardware converter
         if constexpr (C::kKind == Kind::Q8) return (float)x * qs.qscale;
         else return small_int_to_float(x) * qs.qscale;
     }
@@ -464,7 +474,9 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
             for (int d = 0; d < 8; ++d) o[d] = fmaf(e[i], r.v[d], o[d]);
         }
     } else {
-        // weights e_i * vs_i as 16-bit fixed point relative to the batch max
+        // weights e_i * vs_i as fixed point relative to the batch max: 15 bits
+        // (q4 / q3) or 13 bits (q8, keeps every 4-row group sum below 2^22)
+        constexpr float kPmax = (C::kKind == Kind::Q8) ? 8191.f : 32767.f;
         float w[R];
         float wmax = 0.f;
 #pragma unroll
@@ -474,52 +486,88 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
             if constexpr (kMasked) w[i] = valid[i] ? w[i] : 0.f;
             wmax = fmaxf(wmax, w[i]);
         }
-        const float inv = wmax > 0.f ? 32767.f / wmax : 0.f;
-        int acc_h[16], acc_l[16];
+        const float inv = wmax > 0.f ? kPmax / wmax : 0.f;
+        // p_i rides in the low bits of 1.5 * 2^23: the float's bit pattern is
+        // 0x4B400000 + p_i, so its low half is p_i
+        uint32_t pb[R];
+        uint32_t psum_u = 0;
 #pragma unroll
-        for (int d = 0; d < 16; ++d) acc_h[d] = acc_l[d] = 0;
-        int psum = 0;
+        for (int i = 0; i < R; ++i) {
+            pb[i] = __float_as_uint(fmaf(w[i], inv, 12582912.0f));
+            psum_u += pb[i] - 0x4B400000u;
+        }
+        const int psum = (int)psum_u;
+        constexpr bool kSignedCodes = C::kKind == Kind::Q8;
+        if constexpr (C::kKind == Kind::Q4) {
+            // raw bytes (two nibbles) transposed once; per byte the dot with the
+            // full byte and with its low nibble give both dims:
+            // hi = (full - lo) / 16
+            int af[8], al[8];
 #pragma unroll
-        for (int g4 = 0; g4 < R / 4; ++g4) {
-            uint32_t ph = 0, pl = 0;
+            for (int k = 0; k < 8; ++k) af[k] = al[k] = 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int pi = float_to_small_int_rn(w[4 * g4 + j] * inv);  // 0..32767
-                psum += pi;
-                ph |= (uint32_t)(pi >> 8) << (8 * j);
-                pl |= (uint32_t)(pi & 0xFF) << (8 * j);
-            }
-            IntWords<C::kKind> rw[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int lr = (rb * R + 4 * g4 + j) * C::kNsg + sg;
-                load_int_words<C::kKind>(rw[j], sV + (size_t)lr * C::kRb + sl * C::kBpl);
-            }
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-                uint32_t t[4];  // t[j]: byte lane j of word wi for rows 0..3
-                transpose4x4(rw[0].w[wi], rw[1].w[wi], rw[2].w[wi], rw[3].w[wi], t);
+            for (int g4 = 0; g4 < R / 4; ++g4) {
+                const uint32_t p01 = __byte_perm(pb[4 * g4], pb[4 * g4 + 1], 0x5410);
+                const uint32_t p23 = __byte_perm(pb[4 * g4 + 2], pb[4 * g4 + 3], 0x5410);
+                uint2 raw[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const int d = word_dim<C::kKind>(wi, j);
-                    if constexpr (C::kKind == Kind::Q8) {
-                        acc_h[d] = dp4a_su(t[j], ph, acc_h[d]);
-                        acc_l[d] = dp4a_su(t[j], pl, acc_l[d]);
-                    } else {
-                        acc_h[d] = dp4a_uu(t[j], ph, acc_h[d]);
-                        acc_l[d] = dp4a_uu(t[j], pl, acc_l[d]);
+                    const int lr = (rb * R + 4 * g4 + j) * C::kNsg + sg;
+                    raw[j] = *reinterpret_cast<const uint2*>(sV + (size_t)lr * C::kRb + sl * C::kBpl);
+                }
+                uint32_t t[8];
+                transpose4x4(raw[0].x, raw[1].x, raw[2].x, raw[3].x, t);
+                transpose4x4(raw[0].y, raw[1].y, raw[2].y, raw[3].y, t + 4);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t tl = t[k] & 0x0F0F0F0Fu;
+                    af[k] = dp2a<false, false, false>(p01, t[k], af[k]);
+                    af[k] = dp2a<true, false, false>(p23, t[k], af[k]);
+                    al[k] = dp2a<false, false, false>(p01, tl, al[k]);
+                    al[k] = dp2a<true, false, false>(p23, tl, al[k]);
+                }
+            }
+            const float wscale = wmax * (1.f / kPmax);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int xlo = al[k] - 8 * psum;
+                const int xhi16 = af[k] - al[k] - 128 * psum;  // 16 * (sum of p * hi-nibble value)
+                o[2 * k] = fmaf((float)xlo, wscale, o[2 * k] * c);
+                o[2 * k + 1] = fmaf((float)xhi16, wscale * 0.0625f, o[2 * k + 1] * c);
+            }
+        } else {
+            int acc[16];
+#pragma unroll
+            for (int d = 0; d < 16; ++d) acc[d] = 0;
+#pragma unroll
+            for (int g4 = 0; g4 < R / 4; ++g4) {
+                const uint32_t p01 = __byte_perm(pb[4 * g4], pb[4 * g4 + 1], 0x5410);
+                const uint32_t p23 = __byte_perm(pb[4 * g4 + 2], pb[4 * g4 + 3], 0x5410);
+                IntWords<C::kKind> rw[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int lr = (rb * R + 4 * g4 + j) * C::kNsg + sg;
+                    load_int_words<C::kKind>(rw[j], sV + (size_t)lr * C::kRb + sl * C::kBpl);
+                }
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi) {
+                    uint32_t t[4];  // t[j]: byte lane j of word wi for rows 0..3
+                    transpose4x4(rw[0].w[wi], rw[1].w[wi], rw[2].w[wi], rw[3].w[wi], t);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int d = word_dim<C::kKind>(wi, j);
+                        acc[d] = dp2a<false, false, kSignedCodes>(p01, t[j], acc[d]);
+                        acc[d] = dp2a<true, false, kSignedCodes>(p23, t[j], acc[d]);
                     }
                 }
             }
-        }
-        const int bias = (C::kKind == Kind::Q4) ? 8 * psum : (C::kKind == Kind::Q3) ? 4 * psum : 0;
-        const float wscale = wmax * (1.f / 32767.f);
+            const int bias = (C::kKind == Kind::Q3) ? 4 * psum : 0;
+            const float wscale = wmax * (1.f / kPmax);
 #pragma unroll
-        for (int d = 0; d < 16; ++d) {
-            const int x = acc_h[d] * 256 + acc_l[d] - bias;
-            // q4 / q3: |x| <= 8 rows * 32767 * 15 < 2^22; q8: up to 2^24
-            const float xf = (C::kKind == Kind::Q8) ? (float)x : small_int_to_float(x);
-            o[d] = fmaf(xf, wscale, o[d] * c);
+            for (int d = 0; d < 16; ++d) {
+                // q3: |x| <= 8 * 32767 * 3 < 2^22; q8: |x| <= 4 * 8191 * 127 < 2^22
+                o[d] = fmaf(small_int_to_float(acc[d] - bias), wscale, o[d] * c);
+            }
         }
     }
 }
