@@ -61,6 +61,7 @@ def parse_args():
     ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+",
                     help="formats also timed for the per-format table (empty: none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
     return ap.parse_args()
@@ -346,6 +347,99 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
             "note": "KV cache resident in HBM (decode state); per step q in, output out, sync"}
 
 
+def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768, S=16):
+    """batched grouped-query decode, 64 sequences, 32 query
+    heads over 8 KV heads, per-sequence length uniform in [1024, 32768] from a
+    seed, INT4 cache. tok/s = B tokens per step."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lens = torch.randint(1024, Lmax + 1, (B,), generator=g, dtype=torch.int32)
+    rows = B * Hkv * Lmax
+    gd = torch.Generator(device=dev).manual_seed(seed)
+    bits = FORMAT_BITS[fmt]
+    parts = []
+    for _ in range(2):  # K then V, quantized in slices to bound the fp32 staging
+        codes = torch.empty(rows * D * bits // 8, dtype=torch.uint8, device=dev)
+        scales = torch.empty(rows * (D // 64), dtype=torch.float16, device=dev)
+        step_rows = 1 << 20
+        for r0 in range(0, rows, step_rows):
+            r1 = min(rows, r0 + step_rows)
+            x = torch.randn((r1 - r0) * D, generator=gd, device=dev)
+            va.quantize(x, bits, 1, r1 - r0, D, codes[r0 * D * bits // 8: r1 * D * bits // 8],
+                        scales[r0 * (D // 64): r1 * (D // 64)])
+        parts.append((codes, scales))
+    (K, sK), (V, sV) = parts
+    q = torch.randn(B * Hq * D, generator=gd, device=dev).half()
+    out = torch.empty(B * Hq * D, dtype=torch.float16, device=dev)
+    ws = torch.zeros(va.gqa_workspace_bytes(B, Hq, D, S), dtype=torch.uint8, device=dev)
+    lens_d = lens.to(dev)
+    b = va.DeviceBufs(K, V, sK, sV, q, out, ws)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            va.decode_gqa(fmt, b, lens_d, B, Hq, Hkv, Lmax, D, S, stream)
+    torch.cuda.synchronize(dev)
+    n = max(3, min(steps, 200))
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=stream):
+        for _ in range(n):
+            va.decode_gqa(fmt, b, lens_d, B, Hq, Hkv, Lmax, D, S, stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        gph.replay()
+        e0.record(stream)
+        gph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    nbytes = int(lens.sum()) * Hkv * 2 * (D * bits // 8 + 2 * (D // 64))
+    return {"workload": f"batched GQA decode B={B} Hq={Hq} Hkv={Hkv} D={D} lens~U[1024,{Lmax}] {fmt}",
+            "ms": ms, "tok_s": B * 1e3 / ms, "gbs": nbytes / (ms * 1e6), "bytes": nbytes, "splits": S,
+            "steps": n, "launches_per_step": 1}
+
+
+def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
+    """BASELINE config 3 across GPUs: one sequence of L positions split into
+    contiguous ranges per rank; each rank decodes its range into per-head
+    partials, the partials are all-gathered over NCCL and merged by the
+    combine kernel (strong scaling: total work fixed)."""
+    from voltattn_b200.launcher import SplitL
+    sl = SplitL(L)
+    Lr = sl.local_len
+    K, V, sK, sV = make_cache(va, torch, fmt, Lr, 777 + sl.rank, dev)
+    q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).half()
+    S = S or va.suggest_splits(fmt, H, Lr, D)
+    ws = va.new_workspace(H, D, S, dev)
+    out_local = torch.empty(H * D, dtype=torch.float16, device=dev)
+    partial = torch.empty(H, D + 2, dtype=torch.float32, device=dev)
+    b = va.DeviceBufs(K, V, sK, sV, q, out_local, ws)
+
+    def pfn(j0, j1):
+        va.decode_partial(fmt, b, H, Lr, D, S, partial)
+        return partial
+
+    for _ in range(5):
+        sl.decode(pfn)
+    torch.cuda.synchronize(dev)
+    n = max(5, min(steps, 500))
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        sl.decode(pfn)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"workload": f"split-L decode, one sequence, H={H} D={D} L={L} {fmt} over {world} GPUs "
+                        "(partials all-gathered over NCCL, combine kernel)",
+            "ms": ms, "tok_s": 1e3 / ms, "gbs": algorithmic_bytes(fmt, L) / (ms * 1e6), "steps": n,
+            "scaling": "strong", "launches_per_step": 2}
+
+
 def run_ours(args, rank, world):
     import torch
     import voltattn_b200 as va
@@ -391,6 +485,14 @@ def run_ours(args, rank, world):
             r["vs_f16"] = table["f16"]["ms"] / r["ms"]
     torch.cuda.empty_cache()
     e2e = e2e_leg(va, torch, fmt, L, K, dev, dist, seed)
+    extra = {}
+    if not args.no_extra:
+        if world == 1:
+            extra["gqa_config5"] = gqa_leg(va, torch, dev, K)
+            torch.cuda.empty_cache()
+        else:
+            extra["splitl_config3"] = splitl_leg(va, torch, dev, dist, world, K)
+            torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_leg(L, fmt)
@@ -418,6 +520,7 @@ def run_ours(args, rank, world):
             "gpu_launches": K * launches,
             "clocks": clocks,
             "formats": table,
+            "extra": extra,
         }
         print(json.dumps(line), flush=True)
     if dist:
