@@ -448,6 +448,9 @@ def run_ours(args, rank, world):
     torch.cuda.set_device(dev)
     dist = None
     if world > 1:
+        # keep NCCL's version banner off stdout: rank 0's stdout carries the JSON line
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         import torch.distributed as tdist
         tdist.init_process_group("nccl", device_id=dev)
         dist = tdist
