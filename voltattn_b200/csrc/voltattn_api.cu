@@ -4,12 +4,14 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/voltattn.h"
 #include "common.cuh"
 #include "decode_plain.cuh"
+#include "decode_mma.cuh"
 #include "decode_stream.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
@@ -79,8 +81,67 @@ int stream_ctas_per_sm(int dev, int* out) {
     return VA_OK;
 }
 
+// Which consumer the quantized "+" formats use. Measured on B200: the
+// tensor-core consumer wins for grouped-query decode (G >= 2: 1.8x on the
+// batched config), the integer dot-product consumer for batch-1 multi-head
+// decode (G = 1: ~20 % faster). VOLTATTN_CONSUMER=dp|mma overrides.
+bool use_mma_consumer(int G) {
+    static const int v = [] {
+        const char* e = std::getenv("VOLTATTN_CONSUMER");
+        if (e && std::strcmp(e, "dp") == 0) return 0;
+        if (e && std::strcmp(e, "mma") == 0) return 1;
+        return -1;
+    }();
+    return v < 0 ? G >= 2 : v != 0;
+}
+
+template <class C>
+int mma_ctas_per_sm(int dev, int* out) {
+    static int occ[kMaxDevices] = {0};
+    static std::mutex mu;
+    if (occ[dev] == 0) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ[dev] == 0) {
+            VA_CUDA(cudaFuncSetAttribute(decode_mma_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            int n = 0;
+            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<C>, C::kThreads,
+                                                                  C::kSmemBytes));
+            occ[dev] = std::max(1, n);
+        }
+    }
+    *out = occ[dev];
+    return VA_OK;
+}
+
+template <class C>
+int launch_mma(const DecodeParams& p, cudaStream_t st) {
+    int dev, occ;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    rc = mma_ctas_per_sm<C>(dev, &occ);
+    if (rc) return rc;
+    const long long units = (long long)p.H * p.S;
+    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_mma_kernel<C>, p));
+    return VA_OK;
+}
+
 template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
+    if constexpr (C::kKind != Kind::F16) {
+        if (use_mma_consumer(C::kG)) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
+    }
     int dev, occ;
     int rc = current_device(&dev);
     if (rc) return rc;
