@@ -401,16 +401,18 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
 def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
     """BASELINE config 3 across GPUs: one sequence of L positions split into
     contiguous ranges per rank; each rank decodes its range into per-head
-    partials, the partials are all-gathered over NCCL and merged by the
-    combine kernel (strong scaling: total work fixed)."""
-    from voltattn_b200.launcher import SplitL
-    sl = SplitL(L)
+    partials, which are exchanged and merged (strong scaling: total work
+    fixed). Two exchanges are timed: NCCL all-gather + combine kernel, and the
+    fused peer-memory exchange-and-combine kernel over NVLink."""
+    from voltattn_b200.launcher import SplitL, SplitLPeer
+    sl = SplitLPeer(L, H, D, dev)
     Lr = sl.local_len
     K, V, sK, sV = make_cache(va, torch, fmt, Lr, 777 + sl.rank, dev)
     q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).half()
     S = S or va.suggest_splits(fmt, H, Lr, D)
     ws = va.new_workspace(H, D, S, dev)
     out_local = torch.empty(H * D, dtype=torch.float16, device=dev)
+    out = torch.empty(H * D, dtype=torch.float16, device=dev)
     partial = torch.empty(H, D + 2, dtype=torch.float32, device=dev)
     b = va.DeviceBufs(K, V, sK, sV, q, out_local, ws)
 
@@ -418,26 +420,29 @@ def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
         va.decode_partial(fmt, b, H, Lr, D, S, partial)
         return partial
 
-    for _ in range(5):
-        sl.decode(pfn)
-    torch.cuda.synchronize(dev)
-    n = max(5, min(steps, 500))
-    dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(n):
-        sl.decode(pfn)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / n
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    return {"workload": f"split-L decode, one sequence, H={H} D={D} L={L} {fmt} over {world} GPUs "
-                        "(partials all-gathered over NCCL, combine kernel)",
-            "ms": ms, "tok_s": 1e3 / ms, "gbs": algorithmic_bytes(fmt, L) / (ms * 1e6), "steps": n,
-            "scaling": "strong", "launches_per_step": 2}
+    def timed(step):
+        for _ in range(5):
+            step()
+        torch.cuda.synchronize(dev)
+        n = max(5, min(steps, 500))
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / n], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()), n
+
+    ms_nccl, n = timed(lambda: SplitL.decode(sl, pfn))
+    ms_p2p, _ = timed(lambda: sl.decode_peer(pfn, out))
+    return {"workload": f"split-L decode, one sequence, H={H} D={D} L={L} {fmt} over {world} GPUs",
+            "ms": ms_p2p, "tok_s": 1e3 / ms_p2p, "gbs": algorithmic_bytes(fmt, L) / (ms_p2p * 1e6),
+            "exchange": "fused peer-memory exchange + combine kernel over NVLink (2 launches per step)",
+            "ms_nccl_allgather": ms_nccl, "steps": n, "scaling": "strong", "launches_per_step": 2}
 
 
 def run_ours(args, rank, world):

@@ -138,6 +138,20 @@ VA_API int va_decode(int fmt, const va_bufs* bufs, int H, int L, int D, int S, v
 VA_API int va_decode_partial(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws,
                              size_t ws_bytes, float* partial, void* stream);
 
+/* Split-L exchange over NVLink peer memory, fused with the combine (no
+ * reference counterpart). Each of R ranks (one GPU each) owns a buffer of
+ * va_exchange_buffer_bytes(R, H, D) bytes, zeroed once, mapped into every
+ * rank's address space (e.g. torch symmetric memory); `peer_buffers` is a
+ * host array of the R buffers' device addresses as seen by this process
+ * (peer_buffers[rank] is the local one). One call per decode step, with
+ * epoch = 1, 2, 3, ... the same on all ranks: stores this rank's partial
+ * (float [H][D+2], from va_decode_partial) into every rank's buffer, raises
+ * a per-head flag on each, waits (bounded, ~1 s, then va_device_error) for
+ * all R ranks' partials, and writes the merged fp16 output [H][D]. R <= 8. */
+VA_API size_t va_exchange_buffer_bytes(int R, int H, int D);
+VA_API int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
+                               unsigned epoch, void* out, void* stream);
+
 /* Log-sum-exp merge (combine, src/voltattn.cu:651-672) of R*S slots per head:
  * slots = float [R][H][S][D+2] (R = 1 is the reference's workspace layout; R > 1
  * is R gathered va_decode_partial / workspace blocks, e.g. one per GPU).

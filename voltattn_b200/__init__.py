@@ -60,6 +60,9 @@ def _load():
     lib.va_decode_gqa.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_gqa.restype = i
     lib.va_decode_noalloc.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, vp]; lib.va_decode_noalloc.restype = i
+    lib.va_exchange_buffer_bytes.argtypes = [i, i, i]; lib.va_exchange_buffer_bytes.restype = sz
+    lib.va_exchange_combine.argtypes = [vp, i, i, i, i, C.POINTER(C.c_void_p), C.c_uint, vp, vp]
+    lib.va_exchange_combine.restype = i
     lib.va_device_error.argtypes = [C.POINTER(i)]; lib.va_device_error.restype = i
     return lib
 
@@ -236,6 +239,18 @@ def decode_gqa(fmt, b: DeviceBufs, lens, B: int, Hq: int, Hkv: int, Lmax: int, D
     vb = b.va()
     _check(_lib.va_decode_gqa(int(Fmt.parse(fmt)), C.byref(vb), _ptr(lens), B, Hq, Hkv, Lmax, D, S, _ptr(b.ws),
                               b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)), "decode_gqa")
+
+
+def exchange_buffer_bytes(R: int, H: int, D: int) -> int:
+    return int(_lib.va_exchange_buffer_bytes(R, H, D))
+
+
+def exchange_combine(partial, H: int, D: int, R: int, rank: int, peer_ptrs, epoch: int, out, stream=None):
+    """Split-L exchange over peer memory fused with the combine (see
+    include/voltattn.h, va_exchange_combine). peer_ptrs: R device addresses."""
+    arr = (C.c_void_p * R)(*peer_ptrs)
+    _check(_lib.va_exchange_combine(_ptr(partial), H, D, R, rank, arr, epoch, _ptr(out), _stream_ptr(stream)),
+           "exchange_combine")
 
 
 def device_error() -> int:

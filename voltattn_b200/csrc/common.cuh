@@ -16,6 +16,7 @@ enum DeviceError : int {
     kErrFullWait = 1,   // consumer gave up waiting for a stage to land
     kErrEmptyWait = 2,  // producer gave up waiting for a stage to drain
     kErrDrainWait = 3,  // producer gave up waiting for its in-flight copies
+    kErrPeerWait = 4,   // split-L exchange gave up waiting for a peer's partial
 };
 
 // Wall-clock budget of every spin wait: ~1 s, then the kernel reports an error

@@ -13,6 +13,7 @@
 #include "decode_plain.cuh"
 #include "decode_mma.cuh"
 #include "decode_stream.cuh"
+#include "exchange.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
 
@@ -437,6 +438,30 @@ int va_combine_partials(const float* slots, int R, int H, int S, int D, void* ou
     if (!slots || !out || R < 1 || H < 1 || S < 1 || D < 1 || D > 128) return VA_ERR_INVALID;
     combine_kernel<<<H, kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(slots, R, H, S, D,
                                                                       static_cast<__half*>(out), nullptr, 0);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+size_t va_exchange_buffer_bytes(int R, int H, int D) {
+    if (R < 1 || R > kMaxRanks || H < 1 || D < 1) return 0;
+    const size_t g = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
+    return g + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255);
+}
+
+int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
+                        unsigned epoch, void* out, void* stream) {
+    if (!partial || !peer_buffers || !out || R < 1 || R > kMaxRanks || rank < 0 || rank >= R || H < 1 || D < 1 ||
+        D > 128 || epoch == 0)
+        return VA_ERR_INVALID;
+    const size_t goff = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
+    PeerBuffers pb = {};
+    for (int r = 0; r < R; ++r) {
+        if (!peer_buffers[r] || !aligned16(peer_buffers[r])) return VA_ERR_INVALID;
+        pb.gather[r] = static_cast<float*>(peer_buffers[r]);
+        pb.flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[r]) + goff);
+    }
+    exchange_combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(partial, H, D, R, rank, pb, epoch,
+                                                                              static_cast<__half*>(out));
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }

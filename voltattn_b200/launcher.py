@@ -13,7 +13,9 @@ inside one GPU). Decode shards three ways:
   H=32) are all-gathered over NCCL into this GPU's own memory, and the
   log-sum-exp combine (va_combine_partials) produces the output on every
   rank. This is the reference's split-L combine (src/voltattn.cu:651-672)
-  lifted across GPUs; no kernel reads another GPU's memory.
+  lifted across GPUs. `SplitLPeer` replaces the NCCL gather by one fused
+  kernel over NVLink peer memory (plain stores into the peers' buffers plus
+  per-head flags, no TMA and no multicast).
 
 The local compute is injectable so that the collective orchestration can be
 tested on CPU with the gloo backend.
@@ -101,6 +103,36 @@ class SplitL:
         if combine_fn is None:
             combine_fn = _gpu_combine
         return combine_fn(gathered, H, D2 - 2)
+
+
+class SplitLPeer(SplitL):
+    """SplitL whose partial exchange runs over NVLink peer memory instead of
+    NCCL: one fused kernel per step (va_exchange_combine) stores this rank's
+    partials into every rank's buffer, raises per-head flags, waits for the
+    peers' partials and merges them. Buffers come from torch symmetric
+    memory (mapped into every rank's address space)."""
+
+    def __init__(self, L_total: int, H: int, D: int, device, group=None):
+        super().__init__(L_total, group)
+        import torch.distributed._symmetric_memory as symm_mem
+        import voltattn_b200 as va
+        self.H, self.D = H, D
+        nbytes = va.exchange_buffer_bytes(self.world, H, D)
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        g = self.group if self.group is not None else dist.group.WORLD
+        self.handle = symm_mem.rendezvous(self.buf, g)
+        self.peer_ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+
+    def decode_peer(self, partial_fn: Callable[[int, int], torch.Tensor], out: torch.Tensor, stream=None) -> torch.Tensor:
+        import voltattn_b200 as va
+        partial = partial_fn(self.j0, self.j1)
+        self.epoch += 1
+        va.exchange_combine(partial, self.H, self.D, self.world, self.rank, self.peer_ptrs, self.epoch, out, stream)
+        return out
 
 
 def _gpu_combine(gathered: torch.Tensor, H: int, D: int) -> torch.Tensor:
