@@ -528,12 +528,18 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
                 }
             }
             const float wscale = wmax * (1.f / kPmax);
+            // the running max rarely moves once a chain is warm: skip the
+            // rescale when no chain of the warp needs it
+            if (__any_sync(0xffffffffu, c != 1.f)) {
+#pragma unroll
+                for (int d = 0; d < 16; ++d) o[d] *= c;
+            }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const int xlo = al[k] - 8 * psum;
                 const int xhi16 = af[k] - al[k] - 128 * psum;  // 16 * (sum of p * hi-nibble value)
-                o[2 * k] = fmaf((float)xlo, wscale, o[2 * k] * c);
-                o[2 * k + 1] = fmaf((float)xhi16, wscale * 0.0625f, o[2 * k + 1] * c);
+                o[2 * k] = fmaf((float)xlo, wscale, o[2 * k]);
+                o[2 * k + 1] = fmaf((float)xhi16, wscale * 0.0625f, o[2 * k + 1]);
             }
         } else {
             int acc[16];
@@ -564,9 +570,14 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
             const int bias = (C::kKind == Kind::Q3) ? 4 * psum : 0;
             const float wscale = wmax * (1.f / kPmax);
 #pragma unroll
+            if (__any_sync(0xffffffffu, c != 1.f)) {
+#pragma unroll
+                for (int d = 0; d < 16; ++d) o[d] *= c;
+            }
+#pragma unroll
             for (int d = 0; d < 16; ++d) {
                 // q3: |x| <= 8 * 32767 * 3 < 2^22; q8: |x| <= 4 * 8191 * 127 < 2^22
-                o[d] = fmaf(small_int_to_float(acc[d] - bias), wscale, o[d] * c);
+                o[d] = fmaf(small_int_to_float(acc[d] - bias), wscale, o[d]);
             }
         }
     }
