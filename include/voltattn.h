@@ -167,6 +167,18 @@ VA_API int va_combine_partials(const float* slots, int R, int H, int S, int D, v
 VA_API int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
                        void* stream);
 
+/* KV append for decode loops (no reference counterpart; the reference
+ * quantizes a whole cache once). Quantizes one new row per KV head of each
+ * sequence, x = fp32 [B][Hkv][D], into a cache laid out as for
+ * va_decode_gqa ([B][Hkv][Lcap] rows), at row pos[b] (device int32 [B]) of
+ * every KV head of sequence b, with exactly the arithmetic of va_quantize:
+ * appending rows one at a time produces the same bytes as quantizing the
+ * whole cache at once. bits = 8 / 4 / 3 (codes + fp16 scales) or 16 (fp16
+ * rows, scales unused). Rows with pos[b] outside [0, Lcap) are skipped. The
+ * caller advances its lengths (e.g. lens += 1) for the next decode. */
+VA_API int va_append_kv(int bits, const float* x, void* codes, void* scales, int B, int Hkv, int Lcap, int D,
+                        const int* pos, void* stream);
+
 /* Read-bandwidth ceiling of `device` (probe_ceiling, src/voltattn.cu:935-957),
  * re-derived for HBM3e: streams a `bytes`-byte buffer (0 = 4 GiB) `reps` times
  * (0 = 20) after 3 warm-up passes with each of two kernels (wide vector loads;

@@ -63,6 +63,7 @@ def _load():
     lib.va_exchange_buffer_bytes.argtypes = [i, i, i]; lib.va_exchange_buffer_bytes.restype = sz
     lib.va_exchange_combine.argtypes = [vp, i, i, i, i, C.POINTER(C.c_void_p), C.c_uint, vp, vp]
     lib.va_exchange_combine.restype = i
+    lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_device_error.argtypes = [C.POINTER(i)]; lib.va_device_error.restype = i
     return lib
 
@@ -218,6 +219,14 @@ def quantize(x, bits: int, H: int, L: int, D: int, codes=None, scales=None, stre
         scales = torch.empty(H * L * (D // GROUP), dtype=torch.float16, device=x.device)
     _check(_lib.va_quantize(bits, _ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)), "quantize")
     return codes, scales
+
+
+def append_kv(x, bits: int, codes, scales, B: int, Hkv: int, Lcap: int, D: int, pos, stream=None):
+    """Quantize one new row per KV head of each sequence (x fp32 [B][Hkv][D])
+    into a [B][Hkv][Lcap] cache at row pos[b] (int32 CUDA tensor), bit-exact
+    with quantize() of the whole cache. bits 16 stores fp16 rows."""
+    _check(_lib.va_append_kv(bits, _ptr(x), _ptr(codes), _ptr(scales), B, Hkv, Lcap, D, _ptr(pos),
+                             _stream_ptr(stream)), "append_kv")
 
 
 def probe_ceiling(device: int = 0, nbytes: int = 0, reps: int = 0, method: Optional[int] = None) -> float:

@@ -23,17 +23,18 @@ __device__ __forceinline__ int lrint_narrow(float y) {
     return (int)(unsigned int)(unsigned long long)t;
 }
 
+// One 64-element group, eight consecutive elements per thread (8 lanes per
+// group, lane-aligned): loads, reduces amax over the 8 lanes, quantizes and
+// packs. `src` points at this thread's 8 inputs; element `e0` (a multiple of
+// 8) and scale index `sidx` place the result. All 32 lanes must call it.
 template <int BITS>
-__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
-                                                       __half* __restrict__ scales, long long ngroups) {
+__device__ __forceinline__ void quantize_group_part(const float* src, bool active, int part, long long e0,
+                                                    long long sidx, uint8_t* __restrict__ codes,
+                                                    __half* __restrict__ scales) {
     constexpr int lim = BITS == 8 ? 127 : BITS == 4 ? 7 : 3;
-    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long grp = tid >> 3;
-    const int part = (int)(tid & 7);
-    const bool active = grp < ngroups;
     float v[8];
     if (active) {
-        const float4* p = reinterpret_cast<const float4*>(x + grp * kGroup + part * 8);
+        const float4* p = reinterpret_cast<const float4*>(src);
         const float4 a = __ldg(p), b = __ldg(p + 1);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
         v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
@@ -55,7 +56,6 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i] = max(-lim, min(lim, lrint_narrow(__fdiv_rn(v[i], sh))));
 
-    const long long e0 = grp * kGroup + part * 8;  // first element of this thread
     if constexpr (BITS == 8) {
         uint32_t w0 = 0, w1 = 0;
 #pragma unroll
@@ -78,7 +78,57 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
         dst[1] = (uint8_t)(w >> 8);
         dst[2] = (uint8_t)(w >> 16);
     }
-    if (part == 0) scales[grp] = hs;
+    if (part == 0) scales[sidx] = hs;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
+                                                       __half* __restrict__ scales, long long ngroups) {
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long grp = tid >> 3;
+    const int part = (int)(tid & 7);
+    const bool active = grp < ngroups;
+    quantize_group_part<BITS>(x + (active ? grp * kGroup + part * 8 : 0), active, part, grp * kGroup + part * 8,
+                              grp, codes, scales);
+}
+
+// KV append: new rows x [B*Hkv][D] (one token per sequence) quantized into a
+// cache [B][Hkv][Lcap][D] at row pos[b] of every KV head of sequence b, with
+// the same arithmetic as quantize_kernel (the rows come out exactly as if the
+// whole cache had been quantized at once). BITS = 16 stores fp16 rows.
+template <int BITS>
+__global__ void __launch_bounds__(256) append_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
+                                                     __half* __restrict__ scales, int Hkv, int Lcap, int D,
+                                                     const int* __restrict__ pos, long long nrows) {
+    const int G = D / kGroup;
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long grp = tid >> 3;  // source group: row grp / G, group grp % G
+    const int part = (int)(tid & 7);
+    const long long rs = grp / G;
+    const int gi = (int)(grp - rs * G);
+    const bool active = rs < nrows;
+    long long rd = 0;
+    bool inb = false;
+    if (active) {
+        const int b = (int)(rs / Hkv);
+        const int p = __ldg(pos + b);
+        inb = p >= 0 && p < Lcap;
+        rd = rs * (long long)Lcap + (inb ? p : 0);  // (b*Hkv + kvh)*Lcap + pos[b]
+    }
+    const float* src = x + (active ? rs * D + gi * kGroup + part * 8 : 0);
+    if constexpr (BITS == 16) {
+        if (active && inb) {
+            const float4* p4 = reinterpret_cast<const float4*>(src);
+            const float4 a = __ldg(p4), c = __ldg(p4 + 1);
+            __half2 h[4] = {__floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w), __floats2half2_rn(c.x, c.y),
+                            __floats2half2_rn(c.z, c.w)};
+            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(codes) + rd * D + gi * kGroup + part * 8) =
+                *reinterpret_cast<uint4*>(h);
+        }
+    } else {
+        quantize_group_part<BITS>(src, active && inb, part, rd * D + gi * kGroup + part * 8, rd * G + gi, codes,
+                                  scales);
+    }
 }
 
 }  // namespace va

@@ -484,6 +484,29 @@ int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int 
     return VA_OK;
 }
 
+int va_append_kv(int bits, const float* x, void* codes, void* scales, int B, int Hkv, int Lcap, int D,
+                 const int* pos, void* stream) {
+    if (bits != 16 && bits != 8 && bits != 4 && bits != 3) return VA_ERR_INVALID;
+    if (!x || !codes || !pos || (bits != 16 && !scales) || B < 1 || Hkv < 1 || Lcap < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || !aligned16(codes) || (scales && (reinterpret_cast<uintptr_t>(scales) & 1u)))
+        return VA_ERR_ALIGN;
+    const long long nrows = (long long)B * Hkv;
+    const long long threads = nrows * (D / kGroup) * 8;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* c = static_cast<uint8_t*>(codes);
+    auto* sc = static_cast<__half*>(scales);
+    switch (bits) {
+        case 16: append_kernel<16><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
+        case 8: append_kernel<8><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
+        case 4: append_kernel<4><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
+        default: append_kernel<3><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
+    }
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
 int va_probe_ceiling_method(int device, int method, size_t bytes, int reps, double* gbs) {
     if (!gbs || (method != 0 && method != 1)) return VA_ERR_INVALID;
     if (bytes == 0) bytes = 4ull << 30;
