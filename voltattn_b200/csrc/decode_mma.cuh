@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_mma_kernel(const Decode
     MmaQ<C> mq;
     int cur_h = -1;
     int k = 0;
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    for (int u = unit_begin(nunits), ue = unit_begin(nunits, 1); u < ue; ++u) {
         bool failed = false;
         const UnitGeom gm = unit_geom<C>(p, u);
         if (gm.h != cur_h) {

@@ -106,6 +106,16 @@ struct UnitGeom {
     int ntiles;
 };
 
+// Units of a CTA: with at most one unit per CTA, unit blockIdx.x; with more,
+// a contiguous range (same counts as a round robin, +-1), so consecutive
+// units share a KV stream and per-stream state (the query's fixed-point
+// form) is prepared once per stream instead of once per unit (1.6x on the
+// batched grouped-query config).
+__device__ __forceinline__ int unit_begin(int nunits, int next = 0) {
+    if (nunits <= (int)gridDim.x) return min((int)blockIdx.x + next, nunits);
+    return (int)(((long long)nunits * (blockIdx.x + next)) / gridDim.x);
+}
+
 template <class C>
 __device__ __forceinline__ UnitGeom unit_geom(const DecodeParams& p, int u) {
     UnitGeom g;
@@ -245,7 +255,7 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
     const long long nr8 = p.total_rows & ~7ll;
     const int nunits = p.H * p.S;
     int k = 0;
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    for (int u = unit_begin(nunits), ue = unit_begin(nunits, 1); u < ue; ++u) {
         const UnitGeom g = unit_geom<C>(p, u);
         const long long cend = min((g.r1 + 7) & ~7ll, nr8);
         for (int t = 0; t < g.ntiles; ++t, ++k) {
@@ -640,7 +650,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) decode_stream_kernel(const Dec
     QState<C> qs;
     int cur_h = -1;
     int k = 0;  // CTA tile counter (the producer's sequence)
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    for (int u = unit_begin(nunits), ue = unit_begin(nunits, 1); u < ue; ++u) {
         bool failed = false;
         const UnitGeom g = unit_geom<C>(p, u);
         if (g.h != cur_h) {
