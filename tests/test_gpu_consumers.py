@@ -1,7 +1,8 @@
-"""Both quantized decode consumers stay parity-checked whatever the default
-dispatch picks: the tensor-core (mma) and the integer dot-product (dp)
-consumer each run batch-1 and grouped-query cases against the oracle, in a
-fresh process with VOLTATTN_CONSUMER set (tests/consumer_check.py)."""
+"""Every quantized decode consumer stays parity-checked whatever the default
+dispatch picks: the tensor-core tile kernel (tc, batch-1 D=128 q4+/q8+), the
+grouped-query tensor-core consumer (mma) and the integer dot-product
+consumer (dp) each run batch-1 and grouped-query cases against the oracle,
+in a fresh process with VOLTATTN_CONSUMER set (tests/consumer_check.py)."""
 import os
 import subprocess
 import sys
@@ -13,7 +14,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("consumer", ["mma", "dp"])
+@pytest.mark.parametrize("consumer", ["tc", "mma", "dp"])
 def test_consumer(consumer):
     env = dict(os.environ, VOLTATTN_CONSUMER=consumer)
     r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "consumer_check.py")], env=env,

@@ -8,11 +8,14 @@
 #include <cstring>
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/voltattn.h"
 #include "common.cuh"
 #include "decode_plain.cuh"
 #include "decode_mma.cuh"
 #include "decode_stream.cuh"
+#include "decode_tc.cuh"
 #include "exchange.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
@@ -82,18 +85,28 @@ int stream_ctas_per_sm(int dev, int* out) {
     return VA_OK;
 }
 
-// Which consumer the quantized "+" formats use. Measured on B200: the
-// tensor-core consumer wins for grouped-query decode (G >= 2: 1.8x on the
-// batched config), the integer dot-product consumer for batch-1 multi-head
-// decode (G = 1: ~20 % faster). VOLTATTN_CONSUMER=dp|mma overrides.
-bool use_mma_consumer(int G) {
+// Which consumer the quantized "+" formats use. Measured on B200: for
+// batch-1 multi-head decode (G = 1) at D = 128 the tensor-core tile kernel
+// (decode_tc.cuh); for grouped-query decode (G >= 2) the tensor-core
+// consumer of decode_mma.cuh (1.8x the integer one on the batched config);
+// otherwise the integer dot-product consumer.
+// VOLTATTN_CONSUMER=dp|mma|tc overrides where the choice applies.
+enum class Consumer { kDp, kMma, kTc };
+
+Consumer pick_consumer(Kind k, int D, int G) {
     static const int v = [] {
         const char* e = std::getenv("VOLTATTN_CONSUMER");
         if (e && std::strcmp(e, "dp") == 0) return 0;
         if (e && std::strcmp(e, "mma") == 0) return 1;
+        if (e && std::strcmp(e, "tc") == 0) return 2;
         return -1;
     }();
-    return v < 0 ? G >= 2 : v != 0;
+    const bool tc_ok = G == 1 && D == 128 && (k == Kind::Q4 || k == Kind::Q8);
+    if (v == 0) return Consumer::kDp;
+    if (v == 1) return Consumer::kMma;
+    if (v == 2 && tc_ok) return Consumer::kTc;
+    if (tc_ok) return Consumer::kTc;
+    return G >= 2 ? Consumer::kMma : Consumer::kDp;
 }
 
 template <class C>
@@ -138,10 +151,95 @@ int launch_mma(const DecodeParams& p, cudaStream_t st) {
     return VA_OK;
 }
 
+// ---- tensor-core tile kernel: 2-D tensor maps of the K / V codes ---------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// [rows][row_bytes] uint8 codes, boxes of box_rows full rows, swizzle span =
+// row bytes (64 or 128), zero fill past the last row.
+int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int row_bytes, int box_rows) {
+    const auto enc = tensor_map_encoder();
+    if (!enc) return VA_ERR_UNSUPPORTED;
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)row_bytes, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VA_OK : VA_ERR_UNSUPPORTED;
+}
+
+template <class C>
+int tc_ctas_per_sm(int dev, int* out) {
+    static int occ[kMaxDevices] = {0};
+    static std::mutex mu;
+    if (occ[dev] == 0) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ[dev] == 0) {
+            VA_CUDA(cudaFuncSetAttribute(decode_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            int n = 0;
+            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tc_kernel<C>, C::kThreads,
+                                                                  C::kSmemBytes));
+            occ[dev] = std::max(1, n);
+        }
+    }
+    *out = occ[dev];
+    return VA_OK;
+}
+
+template <class C>
+int launch_tc(const DecodeParams& p, cudaStream_t st) {
+    int dev, occ;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    rc = tc_ctas_per_sm<C>(dev, &occ);
+    if (rc) return rc;
+    CUtensorMap tmK, tmV;
+    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, C::kBox);
+    if (rc) return rc;
+    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, C::kBox);
+    if (rc) return rc;
+    const long long units = (long long)p.H * p.S;
+    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tc_kernel<C>, p, tmK, tmV));
+    return VA_OK;
+}
+
 template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
     if constexpr (C::kKind != Kind::F16) {
-        if (use_mma_consumer(C::kG)) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
+        const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
+        if constexpr (C::kG == 1 && C::kD == 128 && (C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
+            // tensor coordinates are 32-bit
+            // and the query is bulk-copied
+            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
+                (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
+                return launch_tc<TcCfg<C::kKind, 128>>(p, st);
+        }
+        if (c == Consumer::kMma) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
     }
     int dev, occ;
     int rc = current_device(&dev);
@@ -200,7 +298,7 @@ int launch_stream_fmt_g(int fmt, const DecodeParams& p, int D, cudaStream_t st) 
 
 size_t gqa_ws_bytes(int B, int Hq, int Hkv, int D, int S) {
     const size_t slots = (size_t)B * Hq * S * (D + 2) * sizeof(float);
-    return ((slots + 255) & ~(size_t)255) + (((size_t)B * Hkv * sizeof(unsigned) + 255) & ~(size_t)255);
+    return ((slots + 255) & ~(size_t)255) + (((size_t)(B * Hkv + 2) * sizeof(unsigned) + 255) & ~(size_t)255);
 }
 
 template <int BITS>
@@ -376,7 +474,8 @@ int va_last_cuda_error(void) { return t_last_cuda_error; }
 
 size_t va_workspace_bytes(int H, int D, int S) {
     if (H < 1 || S < 1 || D < 1) return 0;
-    return counters_offset(H, D, S) + (((size_t)H * sizeof(unsigned) + 255) & ~(size_t)255);
+    // per-head tickets plus the two words of the dynamic unit schedule
+    return counters_offset(H, D, S) + (((size_t)(H + 2) * sizeof(unsigned) + 255) & ~(size_t)255);
 }
 
 int va_workspace_init(void* ws, size_t bytes, void* stream) {
