@@ -160,6 +160,38 @@ struct TcHeader {
     int unit, tile, ntiles, pad;
 };
 
+// Unit (head h, split s) of the tile kernel: the head's rows [r0, r1) are cut
+// into tiles of kTr rows starting at the 8-row block of r0 (a0), and split s
+// takes tiles s, s + S, s + 2S, ...: a head's splits sweep its rows side by
+// side (the online softmax needs no contiguity), which keeps the copies of
+// all CTAs in a narrow window of the cache like one sequential stream.
+// Tile i of the unit starts at tile_row(g, i); rows outside [r0, r1) are masked.
+struct TcUnit {
+    int h, s, S;
+    long long r0, r1, a0;
+    int ntiles;
+};
+
+template <class C>
+__device__ __forceinline__ TcUnit tc_unit_geom(const DecodeParams& p, int u) {
+    TcUnit g;
+    g.h = u / p.S;
+    g.s = u - g.h * p.S;
+    g.S = p.S;
+    const long long len = p.lens ? (long long)min(max(__ldg(p.lens + g.h / p.Hkv), 0), p.L) : (long long)p.L;
+    g.r0 = (long long)g.h * p.L;
+    g.r1 = g.r0 + len;
+    g.a0 = g.r0 & ~7ll;
+    const int T = len > 0 ? (int)((g.r1 - g.a0 + C::kTr - 1) / C::kTr) : 0;
+    g.ntiles = T > g.s ? (T - g.s + p.S - 1) / p.S : 0;
+    return g;
+}
+
+template <class C>
+__device__ __forceinline__ long long tc_tile_row(const TcUnit& g, int i) {
+    return g.a0 + (long long)(g.s + (long long)i * g.S) * C::kTr;
+}
+
 template <class C>
 __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const CUtensorMap* tmV, uint8_t* stages,
                             TcHeader* hdr, uint8_t* qring, uint64_t* full, uint64_t* empty) {
@@ -189,7 +221,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
     while (ok && u < nunits) {
         int unext = nunits;
         bool asked = false;
-        const UnitGeom g = unit_geom<C>(p, u);
+        const TcUnit g = tc_unit_geom<C>(p, u);
         const long long r1b = (g.r1 + 7) & ~7ll;
         const long long cend = min(r1b, nr8);
         const int nt = max(g.ntiles, 1);
@@ -215,7 +247,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             uint8_t* sV = sK + C::kTr * C::kRb;
             uint8_t* sSK = sV + C::kTr * C::kRb;
             uint8_t* sSV = sSK + C::kTr * C::kSb;
-            const long long t0 = g.a0 + (long long)t * C::kTr;
+            const long long t0 = tc_tile_row<C>(g, t);
             const long long tend = t0 + C::kTr;
             const int need = (int)(min(tend, r1b) - t0);
             const int nbox = (need + C::kBox - 1) / C::kBox;
@@ -593,35 +625,36 @@ __device__ __forceinline__ int tc_out_dim(int pi, int x, int g, int t) {
 
 // Single-pass log-sum-exp merge of a head's S slots (the reference's
 // combine, src/voltattn.cu:651-672) for dims lane + 32 j, j < kJ, by one
-// lane: the loads of a batch of 8 slots are independent, so each batch costs
-// one L2 round trip.
-template <int kJ>
+// lane: the loads of a batch of kB slots are independent, so each batch
+// costs one L2 round trip (one in all for S <= kB).
+template <int kJ, int kB = 16>
 __device__ __forceinline__ void tc_merge_slots(const float* hs, int S, int D, int lane, float& ms, float& ls,
                                                float* od) {
     ms = kNegMax;
     ls = 0.f;
 #pragma unroll
     for (int j = 0; j < kJ; ++j) od[j] = 0.f;
-    for (int i0 = 0; i0 < S; i0 += 8) {
-        float m[8], l[8], o[8][kJ];
+    for (int i0 = 0; i0 < S; i0 += kB) {
+        float m[kB], l[kB], o[kB][kJ];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float* sp = hs + (size_t)min(i0 + i, S - 1) * (D + 2);
-            m[i] = i0 + i < S ? __ldcg(sp) * kLog2e : kNegMax;  // slots hold natural-log m
-            l[i] = __ldcg(sp + 1);
+        for (int i = 0; i < kB; ++i) {
+            const bool in = i0 + i < S;
+            const float* sp = hs + (size_t)(in ? i0 + i : 0) * (D + 2);
+            m[i] = in ? __ldcg(sp) * kLog2e : kNegMax;  // slots hold natural-log m
+            l[i] = in ? __ldcg(sp + 1) : 0.f;
 #pragma unroll
-            for (int j = 0; j < kJ; ++j) o[i][j] = __ldcg(sp + 2 + lane + 32 * j);
+            for (int j = 0; j < kJ; ++j) o[i][j] = in ? __ldcg(sp + 2 + lane + 32 * j) : 0.f;
         }
         float bm = ms;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) bm = fmaxf(bm, m[i]);
+        for (int i = 0; i < kB; ++i) bm = fmaxf(bm, m[i]);
         const float c = fast_exp2(ms - bm);
         ls *= c;
 #pragma unroll
         for (int j = 0; j < kJ; ++j) od[j] *= c;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float a = i0 + i < S ? fast_exp2(m[i] - bm) : 0.f;
+        for (int i = 0; i < kB; ++i) {
+            const float a = fast_exp2(m[i] - bm);  // 0 for the padding (m = -FLT_MAX)
             ls = fmaf(l[i], a, ls);
 #pragma unroll
             for (int j = 0; j < kJ; ++j) od[j] = fmaf(o[i][j], a, od[j]);
@@ -757,7 +790,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     }
     TcQ tq;
     TcState<C> st;
-    UnitGeom gm;
+    TcUnit gm;
     int cur_h = -1;
     if (mbar_wait_bounded(qbar, 0)) {
         tc_load_q<C>(tq, reinterpret_cast<const __half*>(qfirst), g, t, lane);
@@ -798,7 +831,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         if (h.unit < 0) break;
         uint8_t* base = stages + (size_t)stage * C::kStageBytes;
         if (h.tile == 0) {
-            gm = unit_geom<C>(p, h.unit);
+            gm = tc_unit_geom<C>(p, h.unit);
             if (gm.h != cur_h && h.ntiles > 0) {
                 tc_load_q<C>(tq, reinterpret_cast<const __half*>(qring + stage * C::kQBytes), g, t, lane);
                 cur_h = gm.h;
@@ -811,7 +844,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
                 for (int x = 0; x < (C::kKind == Kind::Q4 ? 4 : 2); ++x) st.o[pi][x] = 0.f;
         }
         if (h.ntiles > 0) {
-            const long long t0 = gm.a0 + (long long)h.tile * C::kTr;
+            const long long t0 = tc_tile_row<C>(gm, h.tile);
             const uint32_t sK = smem_u32(base), sV = sK + C::kTr * C::kRb;
             const __half* sSK = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb);
             const __half* sSV = sSK + C::kTr * C::kNgrp;
