@@ -36,11 +36,12 @@ sys.path.insert(0, ROOT)
 H, D = 32, 128
 FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the top kernel at
-# L=16384: the ncu capture of profiles/decode_stream_L65536.md (L=65536, above
-# the L2 size) scaled by the rows processed (x 1/4); reads equal the
-# algorithmic bytes there. Formats without a capture report None.
-NCU_TRAFFIC_BYTES = {"q4+": int((285.380864e6 + 3.994112e6) / 4),
-                     "q8+": int((553.767680e6 + 3.673088e6) / 4),
+# L=16384: the ncu captures of profiles/decode_tc_L65536.md (q4+, q8+: tile
+# kernel) and profiles/decode_stream_L65536.md (f16+: streaming kernel), taken
+# at L=65536 (above the L2 size) and scaled by the rows processed (x 1/4);
+# reads equal the algorithmic bytes there. Formats without a capture report None.
+NCU_TRAFFIC_BYTES = {"q4+": int((285.285120e6 + 3.214080e6) / 4),
+                     "q8+": int((553.715456e6 + 3.673344e6) / 4),
                      "f16+": int((1073.790e6 + 3.593472e6) / 4)}
 
 

@@ -498,13 +498,25 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
         return VA_OK;
     }
     int occ = 1;
-    rc = stream_cfg_occupancy(fmt, D, dev, &occ);
+    int tr;
+    double unit_rows;  // fixed cost of a unit in rows of streaming
+    const bool tc = D == 128 && (fmt == VA_Q4P || fmt == VA_Q8P) &&
+                    pick_consumer(fmt == VA_Q4P ? Kind::Q4 : Kind::Q8, D, 1) == Consumer::kTc;
+    if (tc) {
+        // tile kernel: per-unit query setup, slot and ticket hand-over
+        rc = fmt == VA_Q4P ? tc_ctas_per_sm<TcCfg<Kind::Q4, 128>>(dev, &occ)
+                           : tc_ctas_per_sm<TcCfg<Kind::Q8, 128>>(dev, &occ);
+        tr = fmt == VA_Q4P ? TcCfg<Kind::Q4, 128>::kTr : TcCfg<Kind::Q8, 128>::kTr;
+        unit_rows = 512.0;
+    } else {
+        rc = stream_cfg_occupancy(fmt, D, dev, &occ);
+        tr = stream_cfg_tile_rows(fmt, D);
+        unit_rows = 256.0;
+    }
     if (rc) return rc;
     const long long cap = (long long)nsm * occ;
-    const int tr = stream_cfg_tile_rows(fmt, D);
     // cost ~ (units per CTA) * (rows per unit + a fixed per-unit overhead:
-    // the merge and ticket, worth ~256 rows of streaming); keep units at
-    // least one 8-row block long
+    // the merge and ticket); keep units at least one 8-row block long
     double best = 1e300;
     int bestS = 1;
     const int smax = std::min(65535, std::max(1, (L + 7) / 8));
@@ -512,7 +524,7 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
         const long long units = (long long)H * s;
         const long long per_cta = (units + cap - 1) / cap;
         const int rows = (((L + s - 1) / s) + 7) & ~7;
-        const double cost = (double)per_cta * (rows + 256.0 + 0.5 * tr);
+        const double cost = (double)per_cta * (rows + unit_rows + 0.5 * tr);
         if (cost < best - 1e-9) {
             best = cost;
             bestS = s;
