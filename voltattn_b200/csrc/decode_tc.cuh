@@ -272,7 +272,8 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 const uint32_t bytes =
                     (uint32_t)nbox * 2u * C::kBox * C::kRb + (uint32_t)brows * 2u * C::kSb + qb;
                 mbar_arrive_expect_tx(&full[stage], bytes);
-                if (qb) bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kD, qb, &full[stage], pol);
+                if (qb)  // the stream's kG query heads, contiguous
+                    bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage], pol);
                 for (int b = 0; b < nbox; ++b) {
                     const int y = (int)(t0 + (long long)b * C::kBox);
                     tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, y, &full[stage], pol);
@@ -689,19 +690,22 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
         if (lane == 0) ticket = atomic_add_acq_rel_gpu(&p.counters[h], 1u);
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
         if (ticket == (unsigned)(p.S - 1)) {
-            float ms, ls, od[D / 32];
-            tc_merge_slots<D / 32>(p.ws + (size_t)h * p.S * (D + 2), p.S, D, lane, ms, ls, od);
+            for (int kq = 0; kq < C::kG; ++kq) {  // the stream's query heads
+                const size_t hq = (size_t)h * C::kG + kq;
+                float ms, ls, od[D / 32];
+                tc_merge_slots<D / 32>(p.ws + hq * p.S * (D + 2), p.S, D, lane, ms, ls, od);
 #pragma unroll
-            for (int j = 0; j < D / 32; ++j) {
-                const int d = lane + 32 * j;
-                if (p.out_mode == kOutHalf) {
-                    p.out[(size_t)h * D + d] = __float2half_rn(od[j] / ls);
-                } else {
-                    float* pp = p.partial + (size_t)h * (D + 2);
-                    pp[2 + d] = od[j];
-                    if (d == 0) {
-                        pp[0] = ms;
-                        pp[1] = ls;
+                for (int j = 0; j < D / 32; ++j) {
+                    const int d = lane + 32 * j;
+                    if (p.out_mode == kOutHalf) {
+                        p.out[hq * D + d] = __float2half_rn(od[j] / ls);
+                    } else {
+                        float* pp = p.partial + hq * (D + 2);
+                        pp[2 + d] = od[j];
+                        if (d == 0) {
+                            pp[0] = ms;
+                            pp[1] = ls;
+                        }
                     }
                 }
             }
@@ -762,7 +766,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             // the first unit's query goes out ahead of the tiles, so the
             // consumers prepare it while the tiles are in flight
             mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
-            bulk_g2s(qfirst, p.q + (size_t)h0 * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
+            bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }

@@ -16,6 +16,7 @@
 #include "decode_mma.cuh"
 #include "decode_stream.cuh"
 #include "decode_tc.cuh"
+#include "decode_tcg.cuh"
 #include "exchange.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
@@ -85,11 +86,11 @@ int stream_ctas_per_sm(int dev, int* out) {
     return VA_OK;
 }
 
-// Which consumer the quantized "+" formats use. Measured on B200: for
-// batch-1 multi-head decode (G = 1) at D = 128 the tensor-core tile kernel
-// (decode_tc.cuh); for grouped-query decode (G >= 2) the tensor-core
-// consumer of decode_mma.cuh (1.8x the integer one on the batched config);
-// otherwise the integer dot-product consumer.
+// Which consumer the quantized "+" formats use. Measured on B200: at D = 128
+// the tensor-core tile kernels for batch-1 decode of q4+/q8+ (decode_tc.cuh)
+// and grouped-query decode of q4+ with 4 query heads per KV head
+// (decode_tcg.cuh); for other grouped-query shapes the tensor-core consumer
+// of decode_mma.cuh; otherwise the integer dot-product consumer.
 // VOLTATTN_CONSUMER=dp|mma|tc overrides where the choice applies.
 enum class Consumer { kDp, kMma, kTc };
 
@@ -101,7 +102,7 @@ Consumer pick_consumer(Kind k, int D, int G) {
         if (e && std::strcmp(e, "tc") == 0) return 2;
         return -1;
     }();
-    const bool tc_ok = G == 1 && D == 128 && (k == Kind::Q4 || k == Kind::Q8);
+    const bool tc_ok = D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || (G == 4 && k == Kind::Q4));
     if (v == 0) return Consumer::kDp;
     if (v == 1) return Consumer::kMma;
     if (v == 2 && tc_ok) return Consumer::kTc;
@@ -229,6 +230,53 @@ int launch_tc(const DecodeParams& p, cudaStream_t st) {
 }
 
 template <class C>
+int tcg_ctas_per_sm(int dev, int* out) {
+    static int occ[kMaxDevices] = {0};
+    static std::mutex mu;
+    if (occ[dev] == 0) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ[dev] == 0) {
+            VA_CUDA(cudaFuncSetAttribute(decode_tcg_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            int n = 0;
+            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tcg_kernel<C>, C::kThreads,
+                                                                  C::kSmemBytes));
+            occ[dev] = std::max(1, n);
+        }
+    }
+    *out = occ[dev];
+    return VA_OK;
+}
+
+template <class C>
+int launch_tcg(const DecodeParams& p, cudaStream_t st) {
+    int dev, occ;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    rc = tcg_ctas_per_sm<C>(dev, &occ);
+    if (rc) return rc;
+    CUtensorMap tmK, tmV;
+    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, C::kBox);
+    if (rc) return rc;
+    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, C::kBox);
+    if (rc) return rc;
+    const long long units = (long long)p.H * p.S;
+    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tcg_kernel<C>, p, tmK, tmV));
+    return VA_OK;
+}
+
+template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
     if constexpr (C::kKind != Kind::F16) {
         const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
@@ -238,6 +286,11 @@ int launch_stream(const DecodeParams& p, cudaStream_t st) {
             if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tc<TcCfg<C::kKind, 128>>(p, st);
+        }
+        if constexpr (C::kG == 4 && C::kD == 128 && C::kKind == Kind::Q4) {
+            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
+                (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
+                return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
         }
         if (c == Consumer::kMma) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
     }
