@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
+    ap.add_argument("--gqa-batch", type=int, default=0,
+                    help="with --profile: the batched GQA decode of config 5 with this many sequences instead")
     return ap.parse_args()
 
 
@@ -352,12 +354,10 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
             "note": "KV cache resident in HBM (decode state); per step q in, output out, sync"}
 
 
-def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768, S=4):
-    """BASELINE config 5: batched grouped-query decode, 64 sequences, 32 query
-    heads over 8 KV heads, per-sequence length uniform in [1024, 32768] from a
-    seed, INT4 cache. tok/s = B tokens per step. S = 4 splits per KV stream
-    (2048 units over the grid) measured best for the grouped-query tile
-    kernel (S = 1, 2, 4, 8, 16: 0.354, 0.280, 0.247, 0.256, 0.291 ms)."""
+def make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S):
+    """Synthetic batched grouped-query state: per-sequence lengths uniform in
+    [1024, Lmax] from a seed, K/V drawn on the GPU and packed by the GPU
+    quantizer into a capacity-padded [B][Hkv][Lmax] cache, fp16 q."""
     g = torch.Generator(device="cpu").manual_seed(seed)
     lens = torch.randint(1024, Lmax + 1, (B,), generator=g, dtype=torch.int32)
     rows = B * Hkv * Lmax
@@ -378,8 +378,17 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
     q = torch.randn(B * Hq * D, generator=gd, device=dev).half()
     out = torch.empty(B * Hq * D, dtype=torch.float16, device=dev)
     ws = torch.zeros(va.gqa_workspace_bytes(B, Hq, D, S), dtype=torch.uint8, device=dev)
-    lens_d = lens.to(dev)
-    b = va.DeviceBufs(K, V, sK, sV, q, out, ws)
+    nbytes = int(lens.sum()) * Hkv * 2 * (D * bits // 8 + 2 * (D // 64))
+    return va.DeviceBufs(K, V, sK, sV, q, out, ws), lens.to(dev), nbytes
+
+
+def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768, S=4):
+    """BASELINE config 5: batched grouped-query decode, 64 sequences, 32 query
+    heads over 8 KV heads, per-sequence length uniform in [1024, 32768] from a
+    seed, INT4 cache. tok/s = B tokens per step. S = 4 splits per KV stream
+    (2048 units over the grid) measured best for the grouped-query tile
+    kernel (S = 1, 2, 4, 8, 16: 0.354, 0.280, 0.247, 0.256, 0.291 ms)."""
+    b, lens_d, nbytes = make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S)
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -399,7 +408,6 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
         e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / n
-    nbytes = int(lens.sum()) * Hkv * 2 * (D * bits // 8 + 2 * (D // 64))
     return {"workload": f"batched GQA decode B={B} Hq={Hq} Hkv={Hkv} D={D} lens~U[1024,{Lmax}] {fmt}",
             "ms": ms, "tok_s": B * 1e3 / ms, "gbs": nbytes / (ms * 1e6), "bytes": nbytes, "splits": S,
             "steps": n, "launches_per_step": 1}
@@ -550,6 +558,15 @@ def run_profile(args):
     import voltattn_b200 as va
     dev = torch.device("cuda", 0)
     fmt, L = args.fmt, args.L
+    if args.gqa_batch > 0:
+        B, Hq, Hkv, Lmax, S = args.gqa_batch, 32, 8, 32768, 4
+        b, lens_d, nbytes = make_gqa(va, torch, dev, 4242, fmt, B, Hq, Hkv, Lmax, S)
+        for _ in range(args.warmup + args.steps):
+            va.decode_gqa(fmt, b, lens_d, B, Hq, Hkv, Lmax, D, S)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": fmt, "gqa_batch": B, "bytes": nbytes, "splits": S,
+                          "launches": args.warmup + args.steps, "device_error": va.device_error()}))
+        return
     cache = make_cache(va, torch, fmt, L, 99, dev)
     q = torch.randn(H * D, device=dev).half()
     out = torch.empty(H * D, dtype=torch.float16, device=dev)
