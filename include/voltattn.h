@@ -179,6 +179,27 @@ VA_API int va_quantize(int bits, const float* x, void* codes, void* scales, int 
 VA_API int va_append_kv(int bits, const float* x, void* codes, void* scales, int B, int Hkv, int Lcap, int D,
                         const int* pos, void* stream);
 
+/* Paged-cache forms of va_decode_gqa and va_append_kv (no reference
+ * counterpart). The cache is a pool of num_pages pages; a page holds
+ * page_rows rows of each of the Hkv KV heads: K/V [num_pages][Hkv][page_rows]
+ * rows in format fmt, scales [num_pages][Hkv][page_rows][D/64]. Row j of KV
+ * head k of sequence b lives in page block_table[b * max_pages + j / page_rows]
+ * (device int32 [B][max_pages]) at row j % page_rows. lens: device int32 [B],
+ * 1 <= lens[b] <= max_pages * page_rows. Entries outside [0, num_pages) read
+ * page 0 (decode) or skip the row (append). Supported: D = 128, page_rows a
+ * multiple of 32, q4+ / q8+ with Hq == Hkv and q4+ with Hq == 4 * Hkv (the
+ * tensor-core tile kernels); other shapes return VA_ERR_UNSUPPORTED. q must be
+ * 16-byte aligned. ws as for va_decode_gqa (va_gqa_workspace_bytes). Splits
+ * s of a sequence take its 256-row tiles s, s + S, s + 2S, ... */
+VA_API int va_decode_paged(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, const int* lens,
+                           int B, int Hq, int Hkv, int page_rows, int num_pages, int D, int S, void* ws,
+                           size_t ws_bytes, void* stream);
+/* Appends x = fp32 [B][Hkv][D] at logical row pos[b] of each sequence of a
+ * paged cache, with the arithmetic of va_quantize (bits 16 / 8 / 4 / 3). */
+VA_API int va_append_kv_paged(int bits, const float* x, void* codes, void* scales, const int* block_table,
+                              int max_pages, int B, int Hkv, int page_rows, int num_pages, int D, const int* pos,
+                              void* stream);
+
 /* Read-bandwidth ceiling of `device` (probe_ceiling, src/voltattn.cu:935-957),
  * re-derived for HBM3e: streams a `bytes`-byte buffer (0 = 4 GiB) `reps` times
  * (0 = 20) after 3 warm-up passes with each of two kernels (wide vector loads;

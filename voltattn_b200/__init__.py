@@ -64,6 +64,10 @@ def _load():
     lib.va_exchange_combine.argtypes = [vp, i, i, i, i, C.POINTER(C.c_void_p), C.c_uint, vp, vp]
     lib.va_exchange_combine.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
+    lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
+    lib.va_decode_paged.restype = i
+    lib.va_append_kv_paged.argtypes = [i, vp, vp, vp, vp, i, i, i, i, i, i, vp, vp]
+    lib.va_append_kv_paged.restype = i
     lib.va_device_error.argtypes = [C.POINTER(i)]; lib.va_device_error.restype = i
     return lib
 
@@ -227,6 +231,24 @@ def append_kv(x, bits: int, codes, scales, B: int, Hkv: int, Lcap: int, D: int, 
     with quantize() of the whole cache. bits 16 stores fp16 rows."""
     _check(_lib.va_append_kv(bits, _ptr(x), _ptr(codes), _ptr(scales), B, Hkv, Lcap, D, _ptr(pos),
                              _stream_ptr(stream)), "append_kv")
+
+
+def append_kv_paged(x, bits: int, codes, scales, block_table, max_pages: int, B: int, Hkv: int, page_rows: int,
+                    num_pages: int, D: int, pos, stream=None):
+    """append_kv into a paged cache ([num_pages][Hkv][page_rows] rows; row j of
+    sequence b in page block_table[b][j // page_rows])."""
+    _check(_lib.va_append_kv_paged(bits, _ptr(x), _ptr(codes), _ptr(scales), _ptr(block_table), max_pages, B, Hkv,
+                                   page_rows, num_pages, D, _ptr(pos), _stream_ptr(stream)), "append_kv_paged")
+
+
+def decode_paged(fmt, b: DeviceBufs, block_table, max_pages: int, lens, B: int, Hq: int, Hkv: int, page_rows: int,
+                 num_pages: int, D: int, S: int, stream=None):
+    """Grouped-query / batch decode over a paged cache (block_table int32
+    [B][max_pages], lens int32 [B], CUDA tensors); workspace as decode_gqa."""
+    vb = b.va()
+    _check(_lib.va_decode_paged(int(Fmt.parse(fmt)), C.byref(vb), _ptr(block_table), max_pages, _ptr(lens), B, Hq,
+                                Hkv, page_rows, num_pages, D, S, _ptr(b.ws), b.ws.numel() * b.ws.element_size(),
+                                _stream_ptr(stream)), "decode_paged")
 
 
 def probe_ceiling(device: int = 0, nbytes: int = 0, reps: int = 0, method: Optional[int] = None) -> float:

@@ -66,6 +66,13 @@ struct DecodeParams {
     int out_mode;
     int Hkv;               // KV heads per sequence (== H for batch-1 decode)
     const int* lens;       // per-sequence valid lengths (nullptr: all L)
+    // paged cache (tile kernels only; page_rows == 0: contiguous streams):
+    // row j of KV head hk of sequence b is physical row
+    // (block_table[b * max_pages + j / page_rows] * Hkv + hk) * page_rows + j % page_rows
+    const int* block_table;
+    int max_pages;
+    int page_rows;
+    int num_pages;
 };
 
 // G = query heads per KV head (1: the reference's batch-1 multi-head decode;

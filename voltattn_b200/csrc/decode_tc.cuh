@@ -170,16 +170,26 @@ struct TcUnit {
     int h, s, S;
     long long r0, r1, a0;
     int ntiles;
+    int b, hk;  // sequence and KV head (paged cache)
 };
 
+// Contiguous streams: rows are the flat rows of [H][L]. Paged cache: rows
+// are the sequence's logical positions [0, len); the producer maps each copy
+// box through the block table.
 template <class C>
 __device__ __forceinline__ TcUnit tc_unit_geom(const DecodeParams& p, int u) {
     TcUnit g;
     g.h = u / p.S;
     g.s = u - g.h * p.S;
     g.S = p.S;
-    const long long len = p.lens ? (long long)min(max(__ldg(p.lens + g.h / p.Hkv), 0), p.L) : (long long)p.L;
-    g.r0 = (long long)g.h * p.L;
+    g.b = g.h / p.Hkv;
+    g.hk = g.h - g.b * p.Hkv;
+    long long len = p.lens ? (long long)min(max(__ldg(p.lens + g.b), 0), p.L) : (long long)p.L;
+    if (p.page_rows > 0) {
+        g.r0 = 0;
+    } else {
+        g.r0 = (long long)g.h * p.L;
+    }
     g.r1 = g.r0 + len;
     g.a0 = g.r0 & ~7ll;
     const int T = len > 0 ? (int)((g.r1 - g.a0 + C::kTr - 1) / C::kTr) : 0;
@@ -252,8 +262,9 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             const int need = (int)(min(tend, r1b) - t0);
             const int nbox = (need + C::kBox - 1) / C::kBox;
             const int brows = (int)max(0ll, min(tend, cend) - t0);
+            const bool paged = p.page_rows > 0;
             const long long rg0 = max(t0, nr8), rg1 = min(tend, g.r1);
-            if (rg1 > rg0) {
+            if (!paged && rg1 > rg0) {
                 // scales of the tensor's last partial 8-row block: plain loads
                 constexpr int kG = C::kSb / 2;
                 const int off = (int)(rg0 - t0);
@@ -265,6 +276,43 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
+            }
+            if (paged) {
+                // one box per lane: physical first row through the block table
+                // (a page index outside the pool reads page 0: no wild access)
+                int py = 0;
+                if (lane < nbox) {
+                    const long long yl = t0 + (long long)lane * C::kBox;
+                    const int pg = (int)(yl / p.page_rows);
+                    int pp = pg < p.max_pages ? __ldg(p.block_table + (size_t)g.b * p.max_pages + pg) : 0;
+                    pp = (pp >= 0 && pp < p.num_pages) ? pp : 0;
+                    py = (pp * p.Hkv + g.hk) * p.page_rows + (int)(yl % p.page_rows);
+                }
+                int ys[C::kTr / C::kBox];
+#pragma unroll
+                for (int b = 0; b < C::kTr / C::kBox; ++b) ys[b] = __shfl_sync(0xffffffffu, py, b);
+                if (lane == 0) {
+                    hdr[stage] = TcHeader{u, t, g.ntiles, 0};
+                    const uint32_t qb = t == 0 ? (uint32_t)C::kQBytes : 0u;
+                    mbar_arrive_expect_tx(&full[stage], (uint32_t)nbox * 2u * C::kBox * (C::kRb + C::kSb) + qb);
+                    if (qb)
+                        bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage],
+                                 pol);
+#pragma unroll
+                    for (int b = 0; b < C::kTr / C::kBox; ++b) {
+                        if (b >= nbox) break;
+                        tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, ys[b], &full[stage], pol);
+                        tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, ys[b], &full[stage], pol);
+                        bulk_g2s(sSK + b * C::kBox * C::kSb,
+                                 reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[b] * C::kSb,
+                                 (uint32_t)C::kBox * C::kSb, &full[stage], pol);
+                        bulk_g2s(sSV + b * C::kBox * C::kSb,
+                                 reinterpret_cast<const uint8_t*>(p.scV) + (size_t)ys[b] * C::kSb,
+                                 (uint32_t)C::kBox * C::kSb, &full[stage], pol);
+                    }
+                }
+                __syncwarp();
+                continue;
             }
             if (lane == 0) {
                 hdr[stage] = TcHeader{u, t, g.ntiles, 0};

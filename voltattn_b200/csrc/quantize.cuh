@@ -96,10 +96,17 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
 // cache [B][Hkv][Lcap][D] at row pos[b] of every KV head of sequence b, with
 // the same arithmetic as quantize_kernel (the rows come out exactly as if the
 // whole cache had been quantized at once). BITS = 16 stores fp16 rows.
+// Page map of a paged cache for append_kernel (table == nullptr: the
+// capacity-padded [B][Hkv][Lcap] layout).
+struct PageMap {
+    const int* table;
+    int max_pages, rows, num_pages;
+};
+
 template <int BITS>
 __global__ void __launch_bounds__(256) append_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
                                                      __half* __restrict__ scales, int Hkv, int Lcap, int D,
-                                                     const int* __restrict__ pos, long long nrows) {
+                                                     const int* __restrict__ pos, long long nrows, PageMap pm) {
     const int G = D / kGroup;
     const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long grp = tid >> 3;  // source group: row grp / G, group grp % G
@@ -112,8 +119,17 @@ __global__ void __launch_bounds__(256) append_kernel(const float* __restrict__ x
     if (active) {
         const int b = (int)(rs / Hkv);
         const int p = __ldg(pos + b);
-        inb = p >= 0 && p < Lcap;
-        rd = rs * (long long)Lcap + (inb ? p : 0);  // (b*Hkv + kvh)*Lcap + pos[b]
+        if (pm.table) {
+            // paged: row p of the sequence lives in page table[b][p / rows]
+            const int kvh = (int)(rs - (long long)b * Hkv);
+            const int pg = p >= 0 ? p / pm.rows : -1;
+            const int pp = (pg >= 0 && pg < pm.max_pages) ? __ldg(pm.table + (size_t)b * pm.max_pages + pg) : -1;
+            inb = pp >= 0 && pp < pm.num_pages;
+            rd = inb ? ((long long)pp * Hkv + kvh) * pm.rows + p % pm.rows : 0;
+        } else {
+            inb = p >= 0 && p < Lcap;
+            rd = rs * (long long)Lcap + (inb ? p : 0);  // (b*Hkv + kvh)*Lcap + pos[b]
+        }
     }
     const float* src = x + (active ? rs * D + gi * kGroup + part * 8 : 0);
     if constexpr (BITS == 16) {

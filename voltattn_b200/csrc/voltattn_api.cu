@@ -403,6 +403,10 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.out_mode = mode;
     p.Hkv = H;
     p.lens = nullptr;
+    p.block_table = nullptr;
+    p.max_pages = 0;
+    p.page_rows = 0;
+    p.num_pages = 0;
     return p;
 }
 
@@ -662,10 +666,10 @@ int va_append_kv(int bits, const float* x, void* codes, void* scales, int B, int
     auto* c = static_cast<uint8_t*>(codes);
     auto* sc = static_cast<__half*>(scales);
     switch (bits) {
-        case 16: append_kernel<16><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
-        case 8: append_kernel<8><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
-        case 4: append_kernel<4><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
-        default: append_kernel<3><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows); break;
+        case 16: append_kernel<16><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows, PageMap{}); break;
+        case 8: append_kernel<8><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows, PageMap{}); break;
+        case 4: append_kernel<4><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows, PageMap{}); break;
+        default: append_kernel<3><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, Lcap, D, pos, nrows, PageMap{}); break;
     }
     VA_CUDA(cudaGetLastError());
     return VA_OK;
@@ -772,6 +776,68 @@ int va_decode_gqa(int fmt, const va_bufs* b, const int* lens, int B, int Hq, int
         case 4: return launch_stream_fmt_g<4>(fmt, p, D, st);
         default: return launch_stream_fmt_g<8>(fmt, p, D, st);
     }
+}
+
+int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_pages, const int* lens, int B,
+                    int Hq, int Hkv, int page_rows, int num_pages, int D, int S, void* ws, size_t ws_bytes,
+                    void* stream) {
+    if (!is_valid_fmt(fmt) || !b || !block_table || !lens) return VA_ERR_INVALID;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || max_pages < 1 || page_rows < 1 || num_pages < 1 || S < 1)
+        return VA_ERR_INVALID;
+    const int G = Hq / Hkv;
+    // the tile kernels: q4+ / q8+ batch-1 layout (G = 1), q4+ with G = 4; copy
+    // boxes of 32 rows stay inside a page
+    const bool ok = D == 128 && page_rows % 32 == 0 &&
+                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || (G == 4 && fmt == VA_Q4P)) &&
+                    pick_consumer(fmt == VA_Q8P ? Kind::Q8 : Kind::Q4, D, G) == Consumer::kTc;
+    if (!ok) return VA_ERR_UNSUPPORTED;
+    const long long streams = (long long)B * Hkv;
+    const long long rows = (long long)num_pages * Hkv * page_rows;
+    const long long lmax = (long long)max_pages * page_rows;
+    if (streams * S > INT_MAX / 2 || rows >= (1ll << 31) || lmax > INT_MAX) return VA_ERR_TOO_LARGE;
+    int rc = check_decode_args(fmt, b, (int)streams, (int)std::min<long long>(lmax, INT_MAX), D, S);
+    if (rc) return rc;
+    if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;  // the query is bulk-copied
+    if (!ws || !aligned16(ws) || ws_bytes < gqa_ws_bytes(B, Hq, Hkv, D, S)) return VA_ERR_WORKSPACE;
+    const size_t slots = (size_t)B * Hq * S * (D + 2) * sizeof(float);
+    unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ((slots + 255) & ~(size_t)255));
+    DecodeParams p = make_params(b, (int)streams, (int)lmax, S, static_cast<float*>(ws), counters, kOutHalf, nullptr);
+    p.total_rows = rows;
+    p.Hkv = Hkv;
+    p.lens = lens;
+    p.block_table = block_table;
+    p.max_pages = max_pages;
+    p.page_rows = page_rows;
+    p.num_pages = num_pages;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
+    return fmt == VA_Q4P ? launch_tc<TcCfg<Kind::Q4, 128>>(p, st) : launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
+}
+
+int va_append_kv_paged(int bits, const float* x, void* codes, void* scales, const int* block_table, int max_pages,
+                       int B, int Hkv, int page_rows, int num_pages, int D, const int* pos, void* stream) {
+    if (bits != 16 && bits != 8 && bits != 4 && bits != 3) return VA_ERR_INVALID;
+    if (!x || !codes || !pos || !block_table || (bits != 16 && !scales) || B < 1 || Hkv < 1 || max_pages < 1 ||
+        page_rows < 1 || num_pages < 1)
+        return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || !aligned16(codes) || (scales && (reinterpret_cast<uintptr_t>(scales) & 1u)))
+        return VA_ERR_ALIGN;
+    const long long nrows = (long long)B * Hkv;
+    const long long threads = nrows * (D / kGroup) * 8;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* c = static_cast<uint8_t*>(codes);
+    auto* sc = static_cast<__half*>(scales);
+    const PageMap pm{block_table, max_pages, page_rows, num_pages};
+    switch (bits) {
+        case 16: append_kernel<16><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, 0, D, pos, nrows, pm); break;
+        case 8: append_kernel<8><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, 0, D, pos, nrows, pm); break;
+        case 4: append_kernel<4><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, 0, D, pos, nrows, pm); break;
+        default: append_kernel<3><<<blocks, 256, 0, st>>>(x, c, sc, Hkv, 0, D, pos, nrows, pm); break;
+    }
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
 }
 
 int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* stream) {
