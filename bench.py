@@ -382,6 +382,67 @@ def make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S):
     return va.DeviceBufs(K, V, sK, sV, q, out, ws), lens.to(dev), nbytes
 
 
+def paged_from(torch, dev, b, lens_d, B, Hkv, Lmax, fmt, page_rows, seed):
+    """The same cache scattered into a pool of pages in a seeded random order:
+    K/V [num_pages][Hkv][page_rows] rows, scales alike, block table [B][max_pages]."""
+    bits = FORMAT_BITS[fmt]
+    rb, ng = D * bits // 8, D // 64
+    max_pages = (Lmax + page_rows - 1) // page_rows
+    num_pages = B * max_pages
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    perm = torch.randperm(num_pages, generator=g).to(dev)
+
+    def scatter(t, width):
+        src = t.view(B, Hkv, max_pages, page_rows, width).permute(0, 2, 1, 3, 4).reshape(num_pages, Hkv, page_rows,
+                                                                                           width)
+        pool = torch.empty_like(src)
+        pool.index_copy_(0, perm, src)
+        return pool.reshape(-1)
+
+    pK, pV = scatter(b.K, rb), scatter(b.V, rb)
+    psK = scatter(b.scK.view(torch.uint8), 2 * ng).view(torch.float16)
+    psV = scatter(b.scV.view(torch.uint8), 2 * ng).view(torch.float16)
+    table = perm.view(B, max_pages).to(torch.int32)
+    return pK, pV, psK, psV, table, max_pages, num_pages
+
+
+def paged_leg(va, torch, dev, steps, page_rows=256, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768, S=4):
+    """Config 5 over a paged cache: the same sequences and lengths, the cache in
+    pages of `page_rows` rows at shuffled pool positions (va_decode_paged)."""
+    b, lens_d, nbytes = make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S)
+    pK, pV, psK, psV, table, max_pages, num_pages = paged_from(torch, dev, b, lens_d, B, Hkv, Lmax, fmt, page_rows,
+                                                              seed)
+    pb = va.DeviceBufs(pK, pV, psK, psV, b.q, b.out, b.ws)
+    b.K = b.V = b.scK = b.scV = None  # the contiguous cache is no longer needed
+    stream = torch.cuda.Stream(device=dev)
+
+    def run():
+        va.decode_paged(fmt, pb, table, max_pages, lens_d, B, Hq, Hkv, page_rows, num_pages, D, S, stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            run()
+    torch.cuda.synchronize(dev)
+    n = max(3, min(steps, 200))
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=stream):
+        for _ in range(n):
+            run()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        gph.replay()
+        e0.record(stream)
+        gph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    return {"workload": f"paged GQA decode B={B} Hq={Hq} Hkv={Hkv} D={D} lens~U[1024,{Lmax}] {fmt}, "
+                        f"pages of {page_rows} rows in shuffled order",
+            "ms": ms, "tok_s": B * 1e3 / ms, "gbs": nbytes / (ms * 1e6), "bytes": nbytes, "splits": S,
+            "page_rows": page_rows, "steps": n, "launches_per_step": 1}
+
+
 def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768, S=4):
     """batched grouped-query decode, 64 sequences, 32 query
     heads over 8 KV heads, per-sequence length uniform in [1024, 32768] from a
@@ -512,6 +573,8 @@ def run_ours(args, rank, world):
     if not args.no_extra:
         if world == 1:
             extra["gqa_config5"] = gqa_leg(va, torch, dev, K)
+            torch.cuda.empty_cache()
+            extra["gqa_config5_paged"] = paged_leg(va, torch, dev, K)
             torch.cuda.empty_cache()
         else:
             extra["splitl_config3"] = splitl_leg(va, torch, dev, dist, world, K)

@@ -228,6 +228,19 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         }
         return false;
     };
+    // Paged cache: physical first row of box `lane` of tile t, through the block
+    // table (a page index outside the pool reads page 0: no wild access).
+    const auto paged_row = [&](const TcUnit& g, int t) -> int {
+        if (p.page_rows <= 0 || g.ntiles <= 0) return 0;
+        const long long pt0 = tc_tile_row<C>(g, t);
+        const int pneed = (int)(min(pt0 + C::kTr, (g.r1 + 7) & ~7ll) - pt0);
+        if (lane * C::kBox >= pneed) return 0;
+        const long long yl = pt0 + (long long)lane * C::kBox;
+        const int pg = (int)(yl / p.page_rows);
+        int pp = pg < p.max_pages ? __ldg(p.block_table + (size_t)g.b * p.max_pages + pg) : 0;
+        pp = (pp >= 0 && pp < p.num_pages) ? pp : 0;
+        return (pp * p.Hkv + g.hk) * p.page_rows + (int)(yl % p.page_rows);
+    };
     while (ok && u < nunits) {
         int unext = nunits;
         bool asked = false;
@@ -235,11 +248,16 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         const long long r1b = (g.r1 + 7) & ~7ll;
         const long long cend = min(r1b, nr8);
         const int nt = max(g.ntiles, 1);
+        int py_next = paged_row(g, 0);
         for (int t = 0; t < nt; ++t, ++k) {
             if (!asked && t >= nt - 2) {
                 if (lane == 0) unext = (int)gridDim.x + (int)atomicAdd(&sched[0], 1u);
                 asked = true;
             }
+            // paged cache: the next tile's block-table entries are loaded now,
+            // one tile ahead of their use
+            const int py = py_next;
+            py_next = (t + 1 < nt) ? paged_row(g, t + 1) : 0;
             if (!acquire(k)) {
                 ok = false;
                 break;
@@ -278,16 +296,6 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 __syncwarp();
             }
             if (paged) {
-                // one box per lane: physical first row through the block table
-                // (a page index outside the pool reads page 0: no wild access)
-                int py = 0;
-                if (lane < nbox) {
-                    const long long yl = t0 + (long long)lane * C::kBox;
-                    const int pg = (int)(yl / p.page_rows);
-                    int pp = pg < p.max_pages ? __ldg(p.block_table + (size_t)g.b * p.max_pages + pg) : 0;
-                    pp = (pp >= 0 && pp < p.num_pages) ? pp : 0;
-                    py = (pp * p.Hkv + g.hk) * p.page_rows + (int)(yl % p.page_rows);
-                }
                 int ys[C::kTr / C::kBox];
 #pragma unroll
                 for (int b = 0; b < C::kTr / C::kBox; ++b) ys[b] = __shfl_sync(0xffffffffu, py, b);
@@ -298,17 +306,23 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                     if (qb)
                         bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage],
                                  pol);
+                    int seg = 0;  // first box of the current run of physically contiguous boxes
 #pragma unroll
                     for (int b = 0; b < C::kTr / C::kBox; ++b) {
                         if (b >= nbox) break;
                         tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, ys[b], &full[stage], pol);
                         tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, ys[b], &full[stage], pol);
-                        bulk_g2s(sSK + b * C::kBox * C::kSb,
-                                 reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[b] * C::kSb,
-                                 (uint32_t)C::kBox * C::kSb, &full[stage], pol);
-                        bulk_g2s(sSV + b * C::kBox * C::kSb,
-                                 reinterpret_cast<const uint8_t*>(p.scV) + (size_t)ys[b] * C::kSb,
-                                 (uint32_t)C::kBox * C::kSb, &full[stage], pol);
+                        // scales: one bulk copy per run of contiguous boxes
+                        if (b + 1 == nbox || ys[b + 1] != ys[b] + C::kBox) {
+                            const uint32_t nb = (uint32_t)(b + 1 - seg) * C::kBox * C::kSb;
+                            bulk_g2s(sSK + seg * C::kBox * C::kSb,
+                                     reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[seg] * C::kSb, nb,
+                                     &full[stage], pol);
+                            bulk_g2s(sSV + seg * C::kBox * C::kSb,
+                                     reinterpret_cast<const uint8_t*>(p.scV) + (size_t)ys[seg] * C::kSb, nb,
+                                     &full[stage], pol);
+                            seg = b + 1;
+                        }
                     }
                 }
                 __syncwarp();
