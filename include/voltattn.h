@@ -51,8 +51,10 @@ extern "C" {
 #endif
 
 /* Formats, in the reference's order (src/voltattn.cu:676). The "+" formats run
- * the staged streaming kernel; f16 / q8 / q4 run the plain one-warp-per-position
- * kernel family kept as attribution baselines. */
+ * the staged streaming kernels; f16 / q8 / q4 run the plain one-warp-per-position
+ * kernel family kept as attribution baselines. bf16+ and f8+ have no reference
+ * counterpart: bf16 rows (no scales), and e4m3 fp8 codes with fp16 scales per
+ * 64-element group (va_quantize_f8). */
 typedef enum va_fmt {
     VA_F16 = 0,
     VA_F16P = 1,
@@ -60,7 +62,9 @@ typedef enum va_fmt {
     VA_Q8P = 3,
     VA_Q4 = 4,
     VA_Q4P = 5,
-    VA_Q3P = 6
+    VA_Q3P = 6,
+    VA_BF16P = 7,
+    VA_F8P = 8
 } va_fmt;
 
 typedef enum va_status {
@@ -166,6 +170,13 @@ VA_API int va_combine_partials(const float* slots, int R, int H, int S, int D, v
  * bytes; scales: __half [H][L][D/64]. x must be 16-byte aligned. */
 VA_API int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
                        void* stream);
+
+/* fp8 group quantizer for f8+ (no reference counterpart), the rule of
+ * va_quantize with lim = 448, the largest finite e4m3 value: per 64-element
+ * group s = amax > 0 ? amax / 448 : 1 rounded to fp16, each code the e4m3
+ * value of x / (stored s) rounded to nearest even with saturation to +-448
+ * (nan stays nan). codes: 1 byte per element; scales: __half [H][L][D/64]. */
+VA_API int va_quantize_f8(const float* x, void* codes, void* scales, int H, int L, int D, void* stream);
 
 /* KV append for decode loops (no reference counterpart; the reference
  * quantizes a whole cache once). Quantizes one new row per KV head of each

@@ -54,6 +54,11 @@ class Oracle:
         lib.or_quantize.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p, _u16p]
         lib.or_dequant.argtypes = [_u8p, _u16p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
         lib.or_round_to_half.argtypes = [_f32p, C.c_size_t, _f32p]
+        lib.or_quantize_f8.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _u8p, _u16p]
+        lib.or_dequant_f8.argtypes = [_u8p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
+        lib.or_e4m3_encode_vec.argtypes = [_f32p, C.c_size_t, _u8p]
+        lib.or_e4m3_decode_vec.argtypes = [_u8p, C.c_size_t, _f32p]
+        lib.or_float_to_bf16_vec.argtypes = [_f32p, C.c_size_t, _u16p]
         lib.or_reference.argtypes = [_f32p, _f32p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
         lib.or_reference_mt.argtypes = [_f32p, _f32p, _u16p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
         lib.or_combine.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _u16p]
@@ -107,6 +112,38 @@ class Oracle:
         out = np.empty(H * L * D, np.float32)
         self.lib.or_dequant(np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint16),
                             H, L, D, bits, out)
+        return out
+
+    def quantize_f8(self, x: np.ndarray, H, L, D):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        codes = np.empty(H * L * D, np.uint8)
+        scales = np.empty(H * L * (D // GROUP), np.uint16)
+        self.lib.or_quantize_f8(x, H, L, D, codes, scales)
+        return codes, scales
+
+    def dequant_f8(self, codes, scales, H, L, D) -> np.ndarray:
+        out = np.empty(H * L * D, np.float32)
+        self.lib.or_dequant_f8(np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint16),
+                               H, L, D, out)
+        return out
+
+    def e4m3_encode(self, x) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint8)
+        self.lib.or_e4m3_encode_vec(x, x.size, out)
+        return out
+
+    def e4m3_decode(self, c) -> np.ndarray:
+        c = np.ascontiguousarray(c, np.uint8).ravel()
+        out = np.empty(c.size, np.float32)
+        self.lib.or_e4m3_decode_vec(c, c.size, out)
+        return out
+
+    def f2bf(self, x) -> np.ndarray:
+        """bf16 bit patterns (round to nearest even)."""
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint16)
+        self.lib.or_float_to_bf16_vec(x, x.size, out)
         return out
 
     def round_to_half(self, x) -> np.ndarray:

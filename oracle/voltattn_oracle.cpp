@@ -10,6 +10,11 @@
 //   * the split-L log-sum-exp combine         (src/voltattn.cu:651-672)
 //   * a grouped-query / variable-length extension of `reference` (no counterpart
 //     in the reference: query head h reads KV head h / group, per sequence).
+//   * the f8+ / bf16+ formats (no counterpart in the reference): an e4m3 fp8
+//     encoder / decoder written from the format's definition (1 sign, 4
+//     exponent bits with bias 7, 3 mantissa bits, no infinities, the all-ones
+//     pattern is nan, largest finite 448) with round-to-nearest-even and
+//     saturation, the f8 group quantizer, and bf16 round-to-nearest-even.
 //
 // Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load
 // this library, and only as the checker. The product (voltattn_b200/) never
@@ -203,6 +208,79 @@ void or_quantize(const float* x, int H, int L, int D, int bits, uint8_t* codes, 
                 codes[byte0 + (bo >> 3)] |= (uint8_t)enc;
                 if ((bo & 7) + 3 > 8) codes[byte0 + (bo >> 3) + 1] |= (uint8_t)(enc >> 8);
             }
+        }
+    }
+}
+
+// e4m3: round to nearest even, saturating to +-448; nan -> 0x7F.
+static uint8_t e4m3_encode(float x) {
+    if (std::isnan(x)) return 0x7F;
+    const uint8_t sign = std::signbit(x) ? 0x80 : 0x00;
+    const float a = std::fabs(x);
+    if (a >= 448.f) return sign | 0x7E;  // the largest finite value (inf included)
+    if (a < 0.015625f) {                 // below 2^-6: subnormals, step 2^-9
+        // m in [0, 8]; m == 8 is the smallest normal 2^-6 whose code is also 8
+        return sign | (uint8_t)std::nearbyint(a * 512.f);
+    }
+    int e;
+    std::frexp(a, &e);  // a = f 2^e, f in [0.5, 1): a's exponent is e - 1
+    int E = e - 1 + 7;
+    float r = std::nearbyint(std::ldexp(a, -(e - 1)) * 8.f);  // 8..16
+    if (r == 16.f) {
+        r = 8.f;
+        ++E;
+    }
+    return sign | (uint8_t)((E << 3) | ((int)r - 8));
+}
+
+static float e4m3_decode(uint8_t c) {
+    const int E = (c >> 3) & 15, M = c & 7;
+    if (E == 15 && M == 7) return NAN;
+    const float v = E == 0 ? std::ldexp((float)M, -9) : std::ldexp(1.f + (float)M / 8.f, E - 7);
+    return (c & 0x80) ? -v : v;
+}
+
+// f8+ group quantizer: the rule of or_quantize with lim = 448 and e4m3 codes.
+void or_quantize_f8(const float* x, int H, int L, int D, uint8_t* codes, uint16_t* scales) {
+    const int G = D / kGroup;
+    for (size_t rowg = 0; rowg < (size_t)H * L * G; ++rowg) {
+        const size_t base = (rowg / G) * D + (rowg % G) * kGroup;
+        float amax = 0.f;
+        for (int i = 0; i < kGroup; ++i) amax = std::max(amax, std::fabs(x[base + i]));
+        const float s = amax > 0.f ? amax / 448.f : 1.f;
+        scales[rowg] = float_to_half_bits(s);
+        const float sh = half_bits_to_float(scales[rowg]);
+        for (int i = 0; i < kGroup; ++i) codes[base + i] = e4m3_encode(x[base + i] / sh);
+    }
+}
+
+void or_dequant_f8(const uint8_t* codes, const uint16_t* scales, int H, int L, int D, float* out) {
+    const int G = D / kGroup;
+    const size_t n = (size_t)H * L * D;
+    for (size_t idx = 0; idx < n; ++idx) {
+        const size_t rowg = (idx / D) * G + (idx % D) / kGroup;
+        out[idx] = (float)((double)half_bits_to_float(scales[rowg]) * (double)e4m3_decode(codes[idx]));
+    }
+}
+
+void or_e4m3_encode_vec(const float* x, size_t n, uint8_t* out) {
+    for (size_t i = 0; i < n; ++i) out[i] = e4m3_encode(x[i]);
+}
+
+void or_e4m3_decode_vec(const uint8_t* c, size_t n, float* out) {
+    for (size_t i = 0; i < n; ++i) out[i] = e4m3_decode(c[i]);
+}
+
+// bf16 round-to-nearest-even (nan stays a quiet nan): bit patterns and values.
+void or_float_to_bf16_vec(const float* x, size_t n, uint16_t* out) {
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t u;
+        std::memcpy(&u, &x[i], 4);
+        if ((u & 0x7FFFFFFFu) > 0x7F800000u) {
+            out[i] = (uint16_t)((u >> 16) | 0x40u);
+        } else {
+            u += 0x7FFFu + ((u >> 16) & 1u);
+            out[i] = (uint16_t)(u >> 16);
         }
     }
 }

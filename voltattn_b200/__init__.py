@@ -64,6 +64,7 @@ def _load():
     lib.va_exchange_combine.argtypes = [vp, i, i, i, i, C.POINTER(C.c_void_p), C.c_uint, vp, vp]
     lib.va_exchange_combine.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
+    lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_paged.restype = i
     lib.va_append_kv_paged.argtypes = [i, vp, vp, vp, vp, i, i, i, i, i, i, vp, vp]
@@ -99,6 +100,8 @@ class Fmt(enum.IntEnum):
     Q4 = 4
     Q4M = 5
     Q3M = 6
+    BF16M = 7  # bf16+ (no reference counterpart)
+    F8M = 8    # f8+: e4m3 codes with fp16 group scales (no reference counterpart)
 
     @property
     def name_str(self) -> str:
@@ -116,7 +119,8 @@ class Fmt(enum.IntEnum):
         return cls(v)
 
 
-FORMATS = [Fmt(i) for i in range(7)]
+FORMATS = [Fmt(i) for i in range(7)]  # the reference's formats
+EXTRA_FORMATS = [Fmt.BF16M, Fmt.F8M]
 
 
 def fmt_name(f) -> str:
@@ -129,7 +133,7 @@ def is_f16(f) -> bool:
 
 def qbits(f) -> int:
     """Quantization bits of a quantized format (src/voltattn.cu:691)."""
-    return {Fmt.Q8: 8, Fmt.Q8M: 8, Fmt.Q4: 4, Fmt.Q4M: 4, Fmt.Q3M: 3}.get(Fmt.parse(f), 8)
+    return {Fmt.Q8: 8, Fmt.Q8M: 8, Fmt.Q4: 4, Fmt.Q4M: 4, Fmt.Q3M: 3, Fmt.F8M: 8}.get(Fmt.parse(f), 8)
 
 
 def qbytes(bits: int, n: int) -> int:
@@ -231,6 +235,18 @@ def append_kv(x, bits: int, codes, scales, B: int, Hkv: int, Lcap: int, D: int, 
     with quantize() of the whole cache. bits 16 stores fp16 rows."""
     _check(_lib.va_append_kv(bits, _ptr(x), _ptr(codes), _ptr(scales), B, Hkv, Lcap, D, _ptr(pos),
                              _stream_ptr(stream)), "append_kv")
+
+
+def quantize_f8(x, H: int, L: int, D: int, codes=None, scales=None, stream=None):
+    """GPU fp8 (e4m3) group quantizer for f8+: fp32 [H][L][D] -> 1-byte codes
+    and fp16 scales [H][L][D/64] (allocated when not given)."""
+    import torch
+    if codes is None:
+        codes = torch.empty(H * L * D, dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty(H * L * (D // 64), dtype=torch.float16, device=x.device)
+    _check(_lib.va_quantize_f8(_ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)), "quantize_f8")
+    return codes, scales
 
 
 def append_kv_paged(x, bits: int, codes, scales, block_table, max_pages: int, B: int, Hkv: int, page_rows: int,

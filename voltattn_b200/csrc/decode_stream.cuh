@@ -83,16 +83,17 @@ struct StreamCfg {
     static constexpr int kD = D;
     static constexpr int kG = G;
     static constexpr int kBits = KindTraits<K>::kBits;
-    static constexpr int kDpl = (K == Kind::F16) ? 8 : 16;                  // dims per lane
+    static constexpr int kDpl = (K == Kind::F16 || K == Kind::BF16) ? 8 : 16;  // dims per lane
     static constexpr int kLpr = D / kDpl;                                  // lanes per row
     static constexpr int kNsg = 32 / kLpr;                                 // chains per warp
-    static constexpr int kRps = (K == Kind::F16 || K == Kind::Q8) ? 4 : 8;  // rows per chain per tile
+    static constexpr int kRps =
+        (is_float_kind(K) || K == Kind::Q8) ? 4 : 8;  // rows per chain per tile
     static constexpr int kWarps = 8;                                       // consumer warps
     static constexpr int kThreads = (kWarps + 1) * 32;
     static constexpr int kTr = kWarps * kNsg * kRps;  // rows per tile
     static constexpr int kWpg = kWarps / G;           // warps per query head
     static constexpr int kRb = D * kBits / 8;         // code bytes per row
-    static constexpr int kSb = (K == Kind::F16) ? 0 : 2 * (D / kGroup);  // scale bytes per row
+    static constexpr int kSb = (K == Kind::F16 || K == Kind::BF16) ? 0 : 2 * (D / kGroup);  // scale bytes per row
     static constexpr int kBpl = kDpl * kBits / 8;     // code bytes per lane
     static constexpr int kStages = 3;
     static constexpr int kStageBytes = 2 * kTr * kRb + 2 * kTr * kSb;
@@ -238,18 +239,36 @@ __host__ __device__ constexpr int word_dim(int w, int j) {
 
 // ---- f16 lane (fp32 math) ------------------------------------------------------------
 
-struct F16Lane {
-    float v[8];
+template <Kind K>
+struct FloatLane {
+    float v[(K == Kind::F8) ? 16 : 8];
 };
 
-__device__ __forceinline__ void load_f16_lane(F16Lane& r, const uint8_t* p) {
+// One lane's 16 bytes as floats: 8 fp16 values, 8 bf16 values (the upper
+// half of an fp32), or 16 e4m3 codes (CUDA's fp8 -> fp16 conversion, exact).
+template <Kind K>
+__device__ __forceinline__ void load_float_lane(FloatLane<K>& r, const uint8_t* p) {
     const uint4 u = *reinterpret_cast<const uint4*>(p);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        r.v[2 * i] = f.x;
-        r.v[2 * i + 1] = f.y;
+        if constexpr (K == Kind::F16) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            r.v[2 * i] = f.x;
+            r.v[2 * i + 1] = f.y;
+        } else if constexpr (K == Kind::BF16) {
+            r.v[2 * i] = __uint_as_float(w[i] << 16);
+            r.v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const __half2_raw hr =
+                    __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> (16 * j)), __NV_E4M3);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+                r.v[4 * i + 2 * j] = f.x;
+                r.v[4 * i + 2 * j + 1] = f.y;
+            }
+        }
     }
 }
 
@@ -331,7 +350,7 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
 
 template <class C>
 struct QState {
-    float qf[C::kDpl];  // f16: q * log2(e)/sqrt(D)
+    float qf[C::kDpl];  // float kinds: q * log2(e)/sqrt(D)
     uint32_t qp[8];     // integer kinds: q as 16-bit pairs, qp[2w] = byte lanes 0,1 of word w, qp[2w+1] = 2,3
     int qbias;          // q4 / q3: code offset * sum of this lane's fixed-point q
     float qscale;       // 2^-e * log2(e) / sqrt(D)
@@ -344,7 +363,7 @@ __device__ __forceinline__ void load_q(QState<C>& qs, const __half* qh, int sl) 
     float x[C::kDpl];
 #pragma unroll
     for (int d = 0; d < C::kDpl; ++d) x[d] = __half2float(qh[sl * C::kDpl + d]);
-    if constexpr (C::kKind == Kind::F16) {
+    if constexpr (is_float_kind(C::kKind)) {
 #pragma unroll
         for (int d = 0; d < C::kDpl; ++d) qs.qf[d] = x[d] * base;
     } else {
@@ -402,12 +421,12 @@ __device__ __forceinline__ int dp2a(uint32_t a, uint32_t b, int c) {
 // Dot of one lane slice with q (before the group scale), in log2 units.
 template <class C>
 __device__ __forceinline__ float lane_score(const QState<C>& qs, const uint8_t* kp) {
-    if constexpr (C::kKind == Kind::F16) {
-        F16Lane r;
-        load_f16_lane(r, kp);
+    if constexpr (is_float_kind(C::kKind)) {
+        FloatLane<C::kKind> r;
+        load_float_lane<C::kKind>(r, kp);
         float acc = 0.f;
 #pragma unroll
-        for (int d = 0; d < 8; ++d) acc = fmaf(qs.qf[d], r.v[d], acc);
+        for (int d = 0; d < C::kDpl; ++d) acc = fmaf(qs.qf[d], r.v[d], acc);
         return acc;
     } else {
         IntWords<C::kKind> r;
@@ -454,7 +473,7 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
             valid[i] = (r >= r0) && (r < r1);
         }
         float acc = lane_score<C>(qs, sK + (size_t)lr * C::kRb + sl * C::kBpl);
-        if constexpr (C::kKind != Kind::F16) acc *= __half2float(sSK[lr * kG + g]);
+        if constexpr (C::kSb > 0) acc *= __half2float(sSK[lr * kG + g]);
 #pragma unroll
         for (int off = C::kLpr / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
         s[i] = valid[i] ? acc : -INFINITY;
@@ -473,22 +492,25 @@ __device__ __forceinline__ void consume_tile(const uint8_t* stage_base, int rb, 
     }
     l = l * c + esum;
 
-    if constexpr (C::kKind == Kind::F16) {
+    if constexpr (is_float_kind(C::kKind)) {
 #pragma unroll
-        for (int d = 0; d < 8; ++d) o[d] *= c;
+        for (int d = 0; d < C::kDpl; ++d) o[d] *= c;
 #pragma unroll
         for (int i = 0; i < R; ++i) {
             const int lr = (rb * R + i) * C::kNsg + sg;
-            F16Lane r;
-            load_f16_lane(r, sV + (size_t)lr * C::kRb + sl * C::kBpl);
+            FloatLane<C::kKind> r;
+            load_float_lane<C::kKind>(r, sV + (size_t)lr * C::kRb + sl * C::kBpl);
+            float wi = e[i];
+            if constexpr (C::kSb > 0) wi *= __half2float(sSV[lr * kG + g]);  // fp8: the group scale
             if constexpr (kMasked) {
                 if (!valid[i]) {
+                    wi = 0.f;
 #pragma unroll
-                    for (int d = 0; d < 8; ++d) r.v[d] = 0.f;
+                    for (int d = 0; d < C::kDpl; ++d) r.v[d] = 0.f;
                 }
             }
 #pragma unroll
-            for (int d = 0; d < 8; ++d) o[d] = fmaf(e[i], r.v[d], o[d]);
+            for (int d = 0; d < C::kDpl; ++d) o[d] = fmaf(wi, r.v[d], o[d]);
         }
     } else {
         // weights e_i * vs_i as fixed point relative to the batch max: 15 bits

@@ -11,7 +11,13 @@
 
 namespace va {
 
-enum class Kind : int { F16 = 0, Q8 = 1, Q4 = 2, Q3 = 3 };
+enum class Kind : int { F16 = 0, Q8 = 1, Q4 = 2, Q3 = 3, BF16 = 4, F8 = 5 };
+
+// Kinds decoded in floating point by the streaming kernel: fp16 and bf16 rows
+// (no scales) and fp8 e4m3 codes with per-group fp16 scales.
+__host__ __device__ constexpr bool is_float_kind(Kind k) {
+    return k == Kind::F16 || k == Kind::BF16 || k == Kind::F8;
+}
 
 template <Kind K>
 struct KindTraits;
@@ -35,6 +41,16 @@ template <>
 struct KindTraits<Kind::Q3> {
     static constexpr int kBits = 3;
     static constexpr int kDpl = 32;
+};
+template <>
+struct KindTraits<Kind::BF16> {
+    static constexpr int kBits = 16;
+    static constexpr int kDpl = 16;
+};
+template <>
+struct KindTraits<Kind::F8> {
+    static constexpr int kBits = 8;
+    static constexpr int kDpl = 16;
 };
 
 // Raw bytes of one lane's DPL dims: 32 B (f16), 16 B (q8, q4), 12 B (q3).

@@ -23,6 +23,12 @@ __device__ __forceinline__ int lrint_narrow(float y) {
     return (int)(unsigned int)(unsigned long long)t;
 }
 
+// BITS value of the fp8 format (f8+, no reference counterpart): e4m3 codes
+// with the same group rule, lim = 448 (the largest finite e4m3 value):
+// s = amax > 0 ? amax / 448 : 1 stored as fp16, code = e4m3(x / stored s)
+// rounded to nearest even with saturation to +-448 (nan stays nan).
+constexpr int kBitsF8 = -8;
+
 // One 64-element group, eight consecutive elements per thread (8 lanes per
 // group, lane-aligned): loads, reduces amax over the 8 lanes, quantizes and
 // packs. `src` points at this thread's 8 inputs; element `e0` (a multiple of
@@ -31,7 +37,7 @@ template <int BITS>
 __device__ __forceinline__ void quantize_group_part(const float* src, bool active, int part, long long e0,
                                                     long long sidx, uint8_t* __restrict__ codes,
                                                     __half* __restrict__ scales) {
-    constexpr int lim = BITS == 8 ? 127 : BITS == 4 ? 7 : 3;
+    constexpr int lim = BITS == 8 ? 127 : BITS == 4 ? 7 : BITS == kBitsF8 ? 448 : 3;
     float v[8];
     if (active) {
         const float4* p = reinterpret_cast<const float4*>(src);
@@ -52,6 +58,17 @@ __device__ __forceinline__ void quantize_group_part(const float* src, bool activ
     const float s = amax > 0.f ? __fdiv_rn(amax, (float)lim) : 1.f;
     const __half hs = __float2half_rn(s);
     const float sh = __half2float(hs);
+    if constexpr (BITS == kBitsF8) {
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0 |= (uint32_t)__nv_cvt_float_to_fp8(__fdiv_rn(v[i], sh), __NV_SATFINITE, __NV_E4M3) << (8 * i);
+            w1 |= (uint32_t)__nv_cvt_float_to_fp8(__fdiv_rn(v[4 + i], sh), __NV_SATFINITE, __NV_E4M3) << (8 * i);
+        }
+        *reinterpret_cast<uint2*>(codes + e0) = make_uint2(w0, w1);
+        if (part == 0) scales[sidx] = hs;
+        return;
+    }
     int c[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i] = max(-lim, min(lim, lrint_narrow(__fdiv_rn(v[i], sh))));

@@ -38,10 +38,12 @@ int cuda_fail(cudaError_t e) {
         if (e__ != cudaSuccess) return cuda_fail(e__);  \
     } while (0)
 
-bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_Q3P; }
-bool is_f16(int f) { return f == VA_F16 || f == VA_F16P; }
+bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_F8P; }
+bool is_f16(int f) { return f == VA_F16 || f == VA_F16P || f == VA_BF16P; }  // 16-bit rows, no scales
 bool is_plain(int f) { return f == VA_F16 || f == VA_Q8 || f == VA_Q4; }
-int fmt_bits(int f) { return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P) ? 8 : (f == VA_Q3P) ? 3 : 4; }
+int fmt_bits(int f) {
+    return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P || f == VA_F8P) ? 8 : (f == VA_Q3P) ? 3 : 4;
+}
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t slots_bytes(int H, int D, int S) { return (size_t)H * S * (D + 2) * sizeof(float); }
@@ -278,7 +280,7 @@ int launch_tcg(const DecodeParams& p, cudaStream_t st) {
 
 template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
-    if constexpr (C::kKind != Kind::F16) {
+    if constexpr (!is_float_kind(C::kKind)) {
         const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
         if constexpr (C::kG == 1 && C::kD == 128 && (C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
             // tensor coordinates are 32-bit
@@ -325,6 +327,8 @@ int launch_stream_d(const DecodeParams& p, int D, cudaStream_t st) {
 
 int launch_stream_fmt(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
     switch (fmt) {
+        case VA_BF16P: return launch_stream_d<Kind::BF16>(p, D, st);
+        case VA_F8P: return launch_stream_d<Kind::F8>(p, D, st);
         case VA_F16P: return launch_stream_d<Kind::F16>(p, D, st);
         case VA_Q8P: return launch_stream_d<Kind::Q8>(p, D, st);
         case VA_Q4P: return launch_stream_d<Kind::Q4>(p, D, st);
@@ -341,6 +345,8 @@ int launch_stream_dg(const DecodeParams& p, int D, cudaStream_t st) {
 template <int G>
 int launch_stream_fmt_g(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
     switch (fmt) {
+        case VA_BF16P: return launch_stream_dg<Kind::BF16, G>(p, D, st);
+        case VA_F8P: return launch_stream_dg<Kind::F8, G>(p, D, st);
         case VA_F16P: return launch_stream_dg<Kind::F16, G>(p, D, st);
         case VA_Q8P: return launch_stream_dg<Kind::Q8, G>(p, D, st);
         case VA_Q4P: return launch_stream_dg<Kind::Q4, G>(p, D, st);
@@ -412,6 +418,8 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
 
 int stream_cfg_tile_rows(int fmt, int D) {
     switch (fmt) {
+        case VA_BF16P: return D == 128 ? StreamCfg<Kind::BF16, 128>::kTr : StreamCfg<Kind::BF16, 64>::kTr;
+        case VA_F8P: return D == 128 ? StreamCfg<Kind::F8, 128>::kTr : StreamCfg<Kind::F8, 64>::kTr;
         case VA_F16P: return D == 128 ? StreamCfg<Kind::F16, 128>::kTr : StreamCfg<Kind::F16, 64>::kTr;
         case VA_Q8P: return D == 128 ? StreamCfg<Kind::Q8, 128>::kTr : StreamCfg<Kind::Q8, 64>::kTr;
         case VA_Q4P: return D == 128 ? StreamCfg<Kind::Q4, 128>::kTr : StreamCfg<Kind::Q4, 64>::kTr;
@@ -421,6 +429,12 @@ int stream_cfg_tile_rows(int fmt, int D) {
 
 int stream_cfg_occupancy(int fmt, int D, int dev, int* occ) {
     switch (fmt) {
+        case VA_BF16P:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::BF16, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::BF16, 64>>(dev, occ);
+        case VA_F8P:
+            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::F8, 128>>(dev, occ)
+                            : stream_ctas_per_sm<StreamCfg<Kind::F8, 64>>(dev, occ);
         case VA_F16P:
             return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::F16, 128>>(dev, occ)
                             : stream_ctas_per_sm<StreamCfg<Kind::F16, 64>>(dev, occ);
@@ -494,13 +508,13 @@ extern "C" {
 int va_version(void) { return 100; }
 
 const char* va_fmt_name(int fmt) {
-    static const char* names[] = {"f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+"};
+    static const char* names[] = {"f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+", "bf16+", "f8+"};
     return is_valid_fmt(fmt) ? names[fmt] : nullptr;
 }
 
 int va_fmt_from_name(const char* name) {
     if (!name) return -1;
-    for (int f = VA_F16; f <= VA_Q3P; ++f)
+    for (int f = VA_F16; f <= VA_F8P; ++f)
         if (std::strcmp(name, va_fmt_name(f)) == 0) return f;
     return -1;
 }
@@ -648,6 +662,19 @@ int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int 
     if (bits == 8) quantize_kernel<8><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
     else if (bits == 4) quantize_kernel<4><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
     else quantize_kernel<3><<<blocks, 256, 0, st>>>(x, c, s, ngroups);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+int va_quantize_f8(const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {
+    if (!x || !codes || !scales || H < 1 || L < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(codes) & 7u) || (reinterpret_cast<uintptr_t>(scales) & 1u))
+        return VA_ERR_ALIGN;
+    const long long ngroups = (long long)H * L * (D / kGroup);
+    const unsigned blocks = (unsigned)((ngroups * 8 + 255) / 256);
+    quantize_kernel<kBitsF8><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, static_cast<uint8_t*>(codes), static_cast<__half*>(scales), ngroups);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }
