@@ -34,7 +34,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 H, D = 32, 128
-FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3}
+FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3, "bf16+": 16, "f8+": 8}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the top kernel at
 # L=16384: the ncu captures of profiles/decode_tc_L65536.md (q4+, q8+: tile
 # kernel) and profiles/decode_stream_L65536.md (f16+: streaming kernel), taken
@@ -63,7 +63,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--fmt", default="q4+")
     ap.add_argument("--L", type=int, default=16384)
-    ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+",
+    ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+,bf16+,f8+",
                     help="formats also timed for the per-format table (empty: none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
@@ -240,7 +240,12 @@ def make_cache(va, torch, fmt, L, seed, dev):
     kx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
     vx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
     bits = FORMAT_BITS[fmt]
-    if bits == 16:
+    if fmt == "bf16+":
+        K, V, sK, sV = kx.bfloat16(), vx.bfloat16(), None, None
+    elif fmt == "f8+":
+        K, sK = va.quantize_f8(kx, H, L, D)
+        V, sV = va.quantize_f8(vx, H, L, D)
+    elif bits == 16:
         K, V, sK, sV = kx.half(), vx.half(), None, None
     else:
         K, sK = va.quantize(kx, bits, H, L, D)
