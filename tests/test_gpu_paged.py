@@ -64,6 +64,7 @@ CASES = [  # fmt, B, Hq, Hkv, Lmax, page_rows, S
     ("q8+", 3, 4, 4, 777, 96, 3),
     ("q8+", 2, 2, 2, 300, 32, 1),
     ("q4+", 1, 32, 8, 4100, 128, 4),
+    ("q4+", 2, 16, 2, 900, 64, 2),   # 8 query heads per KV head
 ]
 
 

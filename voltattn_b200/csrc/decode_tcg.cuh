@@ -43,26 +43,31 @@ struct TcgCfg {
     static constexpr int kChunks = kRb / 16;
     static constexpr int kNgrp = D / kGroup;
     static constexpr int kSb = 2 * kNgrp;
-    static constexpr int kWarps = 4;
+    static constexpr int kHg = G / 4;        // head groups: 4 query heads per consumer warp
+    static constexpr int kRowWarps = 4;      // warps splitting a tile's rows
+    static constexpr int kWarps = kRowWarps * kHg;
     static constexpr int kRpw = 64;
-    static constexpr int kTr = kWarps * kRpw;
+    static constexpr int kTr = kRowWarps * kRpw;
     static constexpr int kBox = 32;
     static constexpr int kThreads = (kWarps + 2) * 32;
-    static constexpr int kStages = 3;
+    static constexpr int kMinBlocks = kHg == 1 ? 2 : 1;  // CTAs per SM the smem budget is cut for
+    static constexpr int kStages = kHg == 1 ? 3 : 5;
     static constexpr int kTRing = 4;
     static constexpr int kStageBytes = (2 * kTr * kRb + 2 * kTr * kSb + 1023) & ~1023;
     static constexpr int kQBytes = G * D * 2;
     // per warp: weight B fragments [k-step][group][lane] (8 bytes); also the
-    // merge area at a unit's end (2 warps x 32 lanes x 18 floats)
+    // merge area at a unit's end (per head group: 2 warps x 32 lanes x 18 floats)
     static constexpr int kPWarp = 2 * 2 * 32 * 8;
-    static constexpr int kPArea = (kWarps * kPWarp > 2 * 32 * 18 * 4) ? kWarps * kPWarp : 2 * 32 * 18 * 4;
+    static constexpr int kMergeBytes = kHg * 2 * 32 * 18 * 4;
+    static constexpr int kPArea = (kWarps * kPWarp > kMergeBytes) ? kWarps * kPWarp : kMergeBytes;
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * 16 +
                                       kStages * kQBytes + kPArea + 2 * kTRing * 8 + kTRing * 4 + 16 + 16 +
                                       kQBytes;
-    static_assert(K == Kind::Q4 && D == 128 && G == 4, "q4+, D = 128, 4 query heads per KV head");
+    static_assert(K == Kind::Q4 && D == 128 && (G == 4 || G == 8), "q4+, D = 128, 4 or 8 query heads per KV head");
     static_assert(kRb == 64, "64-byte swizzle");
     static_assert((kStages * kStageBytes + 2 * kStages * 8 + kStages * 16) % 16 == 0, "query ring");
     static_assert((kStages * kQBytes + kPArea + 2 * kTRing * 8 + kTRing * 4 + 16) % 16 == 0, "first query");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
 // Row of 16-row block `blk` held by mma row g (A) and g + 8 (B).
@@ -80,7 +85,7 @@ struct TcgQ {
 
 template <class C>
 __device__ __forceinline__ void tcg_load_q(TcgQ& tq, const __half* qs, int g, int t, int lane) {
-    constexpr int D = C::kD, G = C::kG;
+    constexpr int D = C::kD, G = 4;  // the warp's head group
     // per-head exponent and group sums: lane L holds dims 4L..4L+3 of each head
     int e[G];
     float x[G][4];
@@ -319,7 +324,7 @@ __device__ __forceinline__ void tcg_tile(uint32_t sK, uint32_t sV, const __half*
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::kThreads, 2)
+__global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     decode_tcg_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -374,7 +379,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     constexpr int kConsumerThreads = C::kWarps * 32;
     const int g = lane >> 2, t = lane & 3, tid = threadIdx.x;
     uint8_t* sp = shP + warp * C::kPWarp;
-    const int wrow = warp * C::kRpw;
+    const int rw = warp % C::kRowWarps, hg = warp / C::kRowWarps;  // rows of the tile, head group
+    const int wrow = rw * C::kRpw;
     // ldmatrix row of this lane in a 32-row k-step: k = lane (rows of blocks 2ks, 2ks+1)
     uint32_t voff[4];
     {
@@ -390,7 +396,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     TcUnit gm;
     int cur_h = -1;
     if (mbar_wait_bounded(qbar, 0)) {
-        tcg_load_q<C>(tq, reinterpret_cast<const __half*>(qfirst), g, t, lane);
+        tcg_load_q<C>(tq, reinterpret_cast<const __half*>(qfirst) + hg * 4 * D, g, t, lane);
         cur_h = h0;
     } else if (lane == 0) {
         report_error(kErrFullWait);
@@ -424,7 +430,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         if (h.tile == 0) {
             gm = tc_unit_geom<C>(p, h.unit);
             if (gm.h != cur_h && h.ntiles > 0) {
-                tcg_load_q<C>(tq, reinterpret_cast<const __half*>(qring + stage * C::kQBytes), g, t, lane);
+                tcg_load_q<C>(tq, reinterpret_cast<const __half*>(qring + stage * C::kQBytes) + hg * 4 * D, g, t,
+                              lane);
                 cur_h = gm.h;
             }
             st.m = kNegMax;
@@ -454,7 +461,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
         float m = st.m;
-        float* area = reinterpret_cast<float*>(shP);  // [2][32][18]
+        float* area = reinterpret_cast<float*>(shP) + hg * 2 * 32 * 18;  // the head group's [2][32][18]
         const auto put = [&](int slot) {
             float* a = area + (slot * 32 + lane) * 18;
             a[0] = m;
@@ -477,15 +484,15 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             m = ms;
         };
         named_barrier_sync(1, kConsumerThreads);  // all warps done with their staging
-        if (warp >= 2) put(warp - 2);
+        if (rw >= 2) put(rw - 2);
         named_barrier_sync(1, kConsumerThreads);
-        if (warp < 2) take(warp);
+        if (rw < 2) take(rw);
         named_barrier_sync(1, kConsumerThreads);
-        if (warp == 1) put(0);
+        if (rw == 1) put(0);
         named_barrier_sync(1, kConsumerThreads);
-        if (warp == 0) {
+        if (rw == 0) {
             take(0);
-            float* slot = p.ws + (((size_t)gm.h * G + t) * p.S + gm.s) * (D + 2);
+            float* slot = p.ws + (((size_t)gm.h * G + 4 * hg + t) * p.S + gm.s) * (D + 2);
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 const int d0 = 2 * (16 * ch + g), d1 = 2 * (16 * ch + g + 8);

@@ -104,7 +104,8 @@ Consumer pick_consumer(Kind k, int D, int G) {
         if (e && std::strcmp(e, "tc") == 0) return 2;
         return -1;
     }();
-    const bool tc_ok = D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || (G == 4 && k == Kind::Q4));
+    const bool tc_ok =
+        D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || ((G == 4 || G == 8) && k == Kind::Q4));
     if (v == 0) return Consumer::kDp;
     if (v == 1) return Consumer::kMma;
     if (v == 2 && tc_ok) return Consumer::kTc;
@@ -289,10 +290,10 @@ int launch_stream(const DecodeParams& p, cudaStream_t st) {
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tc<TcCfg<C::kKind, 128>>(p, st);
         }
-        if constexpr (C::kG == 4 && C::kD == 128 && C::kKind == Kind::Q4) {
+        if constexpr ((C::kG == 4 || C::kG == 8) && C::kD == 128 && C::kKind == Kind::Q4) {
             if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
-                return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
+                return launch_tcg<TcgCfg<Kind::Q4, 128, C::kG>>(p, st);
         }
         if (c == Consumer::kMma) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
     }
@@ -815,7 +816,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     // the tile kernels: q4+ / q8+ batch-1 layout (G = 1), q4+ with G = 4; copy
     // boxes of 32 rows stay inside a page
     const bool ok = D == 128 && page_rows % 32 == 0 &&
-                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || (G == 4 && fmt == VA_Q4P)) &&
+                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || ((G == 4 || G == 8) && fmt == VA_Q4P)) &&
                     pick_consumer(fmt == VA_Q8P ? Kind::Q8 : Kind::Q4, D, G) == Consumer::kTc;
     if (!ok) return VA_ERR_UNSUPPORTED;
     const long long streams = (long long)B * Hkv;
@@ -838,6 +839,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
+    if (G == 8) return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
     return fmt == VA_Q4P ? launch_tc<TcCfg<Kind::Q4, 128>>(p, st) : launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
 }
 
