@@ -27,6 +27,7 @@ CASES = [  # B, Hq, Hkv, Lmax, D, S
     (4, 16, 2, 1031, 128, 4),
     (2, 16, 2, 513, 64, 1),
     (5, 4, 1, 96, 128, 7),
+    (3, 8, 4, 600, 128, 2),   # 2 query heads per KV head
 ]
 
 

@@ -65,6 +65,7 @@ CASES = [  # fmt, B, Hq, Hkv, Lmax, page_rows, S
     ("q8+", 2, 2, 2, 300, 32, 1),
     ("q4+", 1, 32, 8, 4100, 128, 4),
     ("q4+", 2, 16, 2, 900, 64, 2),   # 8 query heads per KV head
+    ("q4+", 2, 8, 4, 500, 32, 2),    # 2 query heads per KV head
 ]
 
 

@@ -43,7 +43,7 @@ struct TcgCfg {
     static constexpr int kChunks = kRb / 16;
     static constexpr int kNgrp = D / kGroup;
     static constexpr int kSb = 2 * kNgrp;
-    static constexpr int kHg = G / 4;        // head groups: 4 query heads per consumer warp
+    static constexpr int kHg = G < 4 ? 1 : G / 4;  // head groups: 4 query head slots per consumer warp
     static constexpr int kRowWarps = 4;      // warps splitting a tile's rows
     static constexpr int kWarps = kRowWarps * kHg;
     static constexpr int kRpw = 64;
@@ -63,7 +63,8 @@ struct TcgCfg {
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * 16 +
                                       kStages * kQBytes + kPArea + 2 * kTRing * 8 + kTRing * 4 + 16 + 16 +
                                       kQBytes;
-    static_assert(K == Kind::Q4 && D == 128 && (G == 4 || G == 8), "q4+, D = 128, 4 or 8 query heads per KV head");
+    static_assert(K == Kind::Q4 && D == 128 && (G == 2 || G == 4 || G == 8),
+                  "q4+, D = 128, 2, 4 or 8 query heads per KV head (G = 2 leaves 2 of 4 head slots idle)");
     static_assert(kRb == 64, "64-byte swizzle");
     static_assert((kStages * kStageBytes + 2 * kStages * 8 + kStages * 16) % 16 == 0, "query ring");
     static_assert((kStages * kQBytes + kPArea + 2 * kTRing * 8 + kTRing * 4 + 16) % 16 == 0, "first query");
@@ -85,13 +86,14 @@ struct TcgQ {
 
 template <class C>
 __device__ __forceinline__ void tcg_load_q(TcgQ& tq, const __half* qs, int g, int t, int lane) {
-    constexpr int D = C::kD, G = 4;  // the warp's head group
+    constexpr int D = C::kD, G = 4;                      // the warp's head slots
+    constexpr int kActive = C::kG < 4 ? C::kG : 4;       // slots holding a query head (rest: q = 0)
     // per-head exponent and group sums: lane L holds dims 4L..4L+3 of each head
     int e[G];
     float x[G][4];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-        const uint2 w4 = reinterpret_cast<const uint2*>(qs + h * D)[lane];
+        const uint2 w4 = h < kActive ? reinterpret_cast<const uint2*>(qs + h * D)[lane] : make_uint2(0u, 0u);
         const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w4.x));
         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w4.y));
         x[h][0] = a.x;
@@ -132,11 +134,11 @@ __device__ __forceinline__ void tcg_load_q(TcgQ& tq, const __half* qs, int g, in
     for (int h = 0; h < G; ++h)
         if (h == hc) ec = e[h];
     const float scc = __int_as_float((127 + ec) << 23);
-    const uint4* src = reinterpret_cast<const uint4*>(qs + hc * D + 32 * t);
+    const uint4* src = reinterpret_cast<const uint4*>(qs + (hc < kActive ? hc : 0) * D + 32 * t);
     uint32_t we[4], wo[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {  // 8 dims = 4 bytes per 16-byte load
-        const uint4 h = src[c];
+        const uint4 h = hc < kActive ? src[c] : make_uint4(0u, 0u, 0u, 0u);
         const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
         uint32_t ae = 0, ao = 0;
 #pragma unroll
@@ -490,7 +492,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         named_barrier_sync(1, kConsumerThreads);
         if (rw == 1) put(0);
         named_barrier_sync(1, kConsumerThreads);
-        if (rw == 0) {
+        if (rw == 0 && 4 * hg + t < G) {  // idle head slots (G = 2) write nothing
             take(0);
             float* slot = p.ws + (((size_t)gm.h * G + 4 * hg + t) * p.S + gm.s) * (D + 2);
 #pragma unroll

@@ -105,7 +105,7 @@ Consumer pick_consumer(Kind k, int D, int G) {
         return -1;
     }();
     const bool tc_ok =
-        D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || ((G == 4 || G == 8) && k == Kind::Q4));
+        D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || ((G == 2 || G == 4 || G == 8) && k == Kind::Q4));
     if (v == 0) return Consumer::kDp;
     if (v == 1) return Consumer::kMma;
     if (v == 2 && tc_ok) return Consumer::kTc;
@@ -290,7 +290,7 @@ int launch_stream(const DecodeParams& p, cudaStream_t st) {
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tc<TcCfg<C::kKind, 128>>(p, st);
         }
-        if constexpr ((C::kG == 4 || C::kG == 8) && C::kD == 128 && C::kKind == Kind::Q4) {
+        if constexpr ((C::kG == 2 || C::kG == 4 || C::kG == 8) && C::kD == 128 && C::kKind == Kind::Q4) {
             if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tcg<TcgCfg<Kind::Q4, 128, C::kG>>(p, st);
@@ -816,7 +816,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     // the tile kernels: q4+ / q8+ batch-1 layout (G = 1), q4+ with G = 4; copy
     // boxes of 32 rows stay inside a page
     const bool ok = D == 128 && page_rows % 32 == 0 &&
-                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || ((G == 4 || G == 8) && fmt == VA_Q4P)) &&
+                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || ((G == 2 || G == 4 || G == 8) && fmt == VA_Q4P)) &&
                     pick_consumer(fmt == VA_Q8P ? Kind::Q8 : Kind::Q4, D, G) == Consumer::kTc;
     if (!ok) return VA_ERR_UNSUPPORTED;
     const long long streams = (long long)B * Hkv;
@@ -838,6 +838,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     p.page_rows = page_rows;
     p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (G == 2) return launch_tcg<TcgCfg<Kind::Q4, 128, 2>>(p, st);
     if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
     if (G == 8) return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
     return fmt == VA_Q4P ? launch_tc<TcCfg<Kind::Q4, 128>>(p, st) : launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
