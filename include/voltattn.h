@@ -190,6 +190,18 @@ VA_API int va_quantize_f8(const float* x, void* codes, void* scales, int H, int 
 VA_API int va_append_kv(int bits, const float* x, void* codes, void* scales, int B, int Hkv, int Lcap, int D,
                         const int* pos, void* stream);
 
+/* Multi-query decode (no reference counterpart), e.g. verifying Q speculative
+ * tokens: the Q new tokens of each sequence are already appended to the cache
+ * ([B][Hkv][Lmax] rows as for va_decode_gqa, lens[b] counting them), and
+ * token i (0 <= i < Q) of query head h attends to rows [0, lens[b] - (Q-1-i))
+ * of KV head h / (Hq/Hkv): causal among the new tokens. q, out: __half
+ * [B][Hq][Q][D]. Every KV row is streamed once for all (Hq/Hkv) * Q query
+ * slots, which must number 2, 4 or 8; q4+, D = 128 (else VA_ERR_UNSUPPORTED);
+ * q 16-byte aligned; lens[b] >= Q. ws_bytes >= va_gqa_workspace_bytes(B,
+ * Hq * Q, D, S). */
+VA_API int va_decode_multiquery(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Q,
+                                int Lmax, int D, int S, void* ws, size_t ws_bytes, void* stream);
+
 /* Paged-cache forms of va_decode_gqa and va_append_kv (no reference
  * counterpart). The cache is a pool of num_pages pages; a page holds
  * page_rows rows of each of the Hkv KV heads: K/V [num_pages][Hkv][page_rows]

@@ -65,6 +65,8 @@ def _load():
     lib.va_exchange_combine.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
+    lib.va_decode_multiquery.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, vp, sz, vp]
+    lib.va_decode_multiquery.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_paged.restype = i
     lib.va_append_kv_paged.argtypes = [i, vp, vp, vp, vp, i, i, i, i, i, i, vp, vp]
@@ -255,6 +257,16 @@ def append_kv_paged(x, bits: int, codes, scales, block_table, max_pages: int, B:
     sequence b in page block_table[b][j // page_rows])."""
     _check(_lib.va_append_kv_paged(bits, _ptr(x), _ptr(codes), _ptr(scales), _ptr(block_table), max_pages, B, Hkv,
                                    page_rows, num_pages, D, _ptr(pos), _stream_ptr(stream)), "append_kv_paged")
+
+
+def decode_multiquery(fmt, b: DeviceBufs, lens, B: int, Hq: int, Hkv: int, Q: int, Lmax: int, D: int, S: int,
+                      stream=None):
+    """Q new tokens per sequence (already in the cache, counted in lens), each
+    causal among the new tokens; q / out fp16 [B][Hq][Q][D]."""
+    vb = b.va()
+    _check(_lib.va_decode_multiquery(int(Fmt.parse(fmt)), C.byref(vb), _ptr(lens), B, Hq, Hkv, Q, Lmax, D, S,
+                                     _ptr(b.ws), b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)),
+           "decode_multiquery")
 
 
 def decode_paged(fmt, b: DeviceBufs, block_table, max_pages: int, lens, B: int, Hq: int, Hkv: int, page_rows: int,

@@ -73,6 +73,10 @@ struct DecodeParams {
     int max_pages;
     int page_rows;
     int num_pages;
+    // multi-query decode (grouped-query tile kernel): the kG query slots of a
+    // KV stream are (query head, token) pairs, mq tokens per head; token i of
+    // mq sees the stream's rows [0, len - (mq - 1 - i)) (1: plain decode)
+    int mq;
 };
 
 // G = query heads per KV head (1: the reference's batch-1 multi-head decode;

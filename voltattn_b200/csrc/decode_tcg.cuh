@@ -449,10 +449,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
             const __half* sSK = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb);
             const __half* sSV = sSK + C::kTr * C::kNgrp;
             const long long w0 = t0 + wrow;
-            if (w0 >= gm.r0 && w0 + C::kRpw <= gm.r1)
-                tcg_tile<C, false>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, st);
+            // multi-query: this lane's slot is token (4 hg + t) % mq, which sees
+            // mq - 1 - token fewer rows; no masking only where every slot sees the warp's rows
+            const long long r1l = gm.r1 - (p.mq - 1 - (4 * hg + t) % p.mq);
+            if (w0 >= gm.r0 && w0 + C::kRpw <= gm.r1 - (p.mq - 1))
+                tcg_tile<C, false>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, r1l, tq, voff, st);
             else
-                tcg_tile<C, true>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, st);
+                tcg_tile<C, true>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, r1l, tq, voff, st);
         }
         if (lane == 0) mbar_arrive(&empty[stage]);
         if (h.tile < h.ntiles - 1) continue;

@@ -414,6 +414,7 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.max_pages = 0;
     p.page_rows = 0;
     p.num_pages = 0;
+    p.mq = 1;
     return p;
 }
 
@@ -804,6 +805,34 @@ int va_decode_gqa(int fmt, const va_bufs* b, const int* lens, int B, int Hq, int
         case 4: return launch_stream_fmt_g<4>(fmt, p, D, st);
         default: return launch_stream_fmt_g<8>(fmt, p, D, st);
     }
+}
+
+int va_decode_multiquery(int fmt, const va_bufs* b, const int* lens, int B, int Hq, int Hkv, int Q, int Lmax,
+                         int D, int S, void* ws, size_t ws_bytes, void* stream) {
+    if (!is_valid_fmt(fmt) || !b || !lens) return VA_ERR_INVALID;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || Q < 1 || Lmax < 1 || S < 1) return VA_ERR_INVALID;
+    const int slots = (Hq / Hkv) * Q;  // query slots per KV stream: (query head, token)
+    if (fmt != VA_Q4P || D != 128 || (slots != 2 && slots != 4 && slots != 8) ||
+        pick_consumer(Kind::Q4, D, slots) != Consumer::kTc)
+        return VA_ERR_UNSUPPORTED;
+    const long long streams = (long long)B * Hkv;
+    if (streams > INT_MAX / 2) return VA_ERR_INVALID;
+    int rc = check_decode_args(fmt, b, (int)streams, Lmax, D, S);
+    if (rc) return rc;
+    if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;  // the query is bulk-copied
+    if (!ws || !aligned16(ws) || ws_bytes < gqa_ws_bytes(B, Hq * Q, Hkv, D, S)) return VA_ERR_WORKSPACE;
+    const size_t slot_bytes = (size_t)B * Hq * Q * S * (D + 2) * sizeof(float);
+    unsigned* counters =
+        reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ((slot_bytes + 255) & ~(size_t)255));
+    DecodeParams p = make_params(b, (int)streams, Lmax, S, static_cast<float*>(ws), counters, kOutHalf, nullptr);
+    p.Hkv = Hkv;
+    p.lens = lens;
+    p.mq = Q;
+    if (p.total_rows >= (1ll << 31)) return VA_ERR_TOO_LARGE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (slots == 2) return launch_tcg<TcgCfg<Kind::Q4, 128, 2>>(p, st);
+    if (slots == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
+    return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
 }
 
 int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_pages, const int* lens, int B,
