@@ -34,7 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 H, D = 32, 128
-FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3, "bf16+": 16, "f8+": 8}
+FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3, "bf16+": 16, "f8+": 8,
+               "q4c+": 4}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the top kernel at
 # L=16384: the ncu captures of profiles/decode_tc_L65536.md (q4+, q8+: tile
 # kernel) and profiles/decode_stream_L65536.md (f16+: streaming kernel), taken
@@ -51,6 +52,8 @@ def algorithmic_bytes(fmt: str, L: int) -> int:
     n = H * L * D
     bits = FORMAT_BITS[fmt]
     payload = 2 * n if bits == 16 else n if bits == 8 else n // 2 if bits == 4 else n * 3 // 8
+    if fmt == "q4c+":  # K scales per (head, channel), V scales per row
+        return 2 * payload + H * D * 2 + H * L * 2
     scales = 0 if bits == 16 else H * L * (D // 64) * 2
     return 2 * (payload + scales)
 
@@ -63,7 +66,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--fmt", default="q4+")
     ap.add_argument("--L", type=int, default=16384)
-    ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+,bf16+,f8+",
+    ap.add_argument("--table", default="f16,f16+,q8,q8+,q4,q4+,q3+,bf16+,f8+,q4c+",
                     help="formats also timed for the per-format table (empty: none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
@@ -245,6 +248,9 @@ def make_cache(va, torch, fmt, L, seed, dev):
     elif fmt == "f8+":
         K, sK = va.quantize_f8(kx, H, L, D)
         V, sV = va.quantize_f8(vx, H, L, D)
+    elif fmt == "q4c+":
+        K, sK = va.quantize_kchan(kx, 4, H, L, D)
+        V, sV = va.quantize_vtok(vx, 4, H, L, D)
     elif bits == 16:
         K, V, sK, sV = kx.half(), vx.half(), None, None
     else:

@@ -54,7 +54,10 @@ extern "C" {
  * the staged streaming kernels; f16 / q8 / q4 run the plain one-warp-per-position
  * kernel family kept as attribution baselines. bf16+ and f8+ have no reference
  * counterpart: bf16 rows (no scales), and e4m3 fp8 codes with fp16 scales per
- * 64-element group (va_quantize_f8). */
+ * 64-element group (va_quantize_f8). q4c+ (no counterpart either): q4 codes
+ * with K scales per (head, channel) over all positions, scK = __half [H][D]
+ * (va_quantize_kchan), and V scales per row, scV = __half [H][L]
+ * (va_quantize_vtok); batch-1 decode at D = 128 with a fused workspace. */
 typedef enum va_fmt {
     VA_F16 = 0,
     VA_F16P = 1,
@@ -64,7 +67,8 @@ typedef enum va_fmt {
     VA_Q4P = 5,
     VA_Q3P = 6,
     VA_BF16P = 7,
-    VA_F8P = 8
+    VA_F8P = 8,
+    VA_Q4CP = 9
 } va_fmt;
 
 typedef enum va_status {
@@ -177,6 +181,15 @@ VA_API int va_quantize(int bits, const float* x, void* codes, void* scales, int 
  * value of x / (stored s) rounded to nearest even with saturation to +-448
  * (nan stays nan). codes: 1 byte per element; scales: __half [H][L][D/64]. */
 VA_API int va_quantize_f8(const float* x, void* codes, void* scales, int H, int L, int D, void* stream);
+
+/* q4c+ quantizers (bits = 8 or 4), the rule of va_quantize with other groups:
+ * va_quantize_kchan: per (head, channel) over the head's L positions,
+ * scales = __half [H][D]; va_quantize_vtok: per row, scales = __half [H][L].
+ * x = fp32 [H][L][D], 16-byte aligned; codes packed as q8 / q4. */
+VA_API int va_quantize_kchan(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
+                             void* stream);
+VA_API int va_quantize_vtok(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
+                            void* stream);
 
 /* KV append for decode loops (no reference counterpart; the reference
  * quantizes a whole cache once). Quantizes one new row per KV head of each

@@ -54,6 +54,10 @@ class Oracle:
         lib.or_quantize.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p, _u16p]
         lib.or_dequant.argtypes = [_u8p, _u16p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
         lib.or_round_to_half.argtypes = [_f32p, C.c_size_t, _f32p]
+        for fn in ("or_quantize_kchan", "or_quantize_vtok"):
+            getattr(lib, fn).argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p, _u16p]
+        for fn in ("or_dequant_kchan", "or_dequant_vtok"):
+            getattr(lib, fn).argtypes = [_u8p, _u16p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
         lib.or_quantize_f8.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _u8p, _u16p]
         lib.or_dequant_f8.argtypes = [_u8p, _u16p, C.c_int, C.c_int, C.c_int, _f32p]
         lib.or_e4m3_encode_vec.argtypes = [_f32p, C.c_size_t, _u8p]
@@ -112,6 +116,34 @@ class Oracle:
         out = np.empty(H * L * D, np.float32)
         self.lib.or_dequant(np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint16),
                             H, L, D, bits, out)
+        return out
+
+    def quantize_kchan(self, x: np.ndarray, H, L, D, bits):
+        """q4c+ K: scales per (head, channel) over the head's L positions, [H][D]."""
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        codes = np.zeros(payload_bytes(bits, H * L * D), np.uint8)
+        scales = np.empty(H * D, np.uint16)
+        self.lib.or_quantize_kchan(x, H, L, D, bits, codes, scales)
+        return codes, scales
+
+    def quantize_vtok(self, x: np.ndarray, H, L, D, bits):
+        """q4c+ V: one scale per row, [H][L]."""
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        codes = np.zeros(payload_bytes(bits, H * L * D), np.uint8)
+        scales = np.empty(H * L, np.uint16)
+        self.lib.or_quantize_vtok(x, H, L, D, bits, codes, scales)
+        return codes, scales
+
+    def dequant_kchan(self, codes, scales, H, L, D, bits) -> np.ndarray:
+        out = np.empty(H * L * D, np.float32)
+        self.lib.or_dequant_kchan(np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint16),
+                                  H, L, D, bits, out)
+        return out
+
+    def dequant_vtok(self, codes, scales, H, L, D, bits) -> np.ndarray:
+        out = np.empty(H * L * D, np.float32)
+        self.lib.or_dequant_vtok(np.ascontiguousarray(codes, np.uint8), np.ascontiguousarray(scales, np.uint16),
+                                 H, L, D, bits, out)
         return out
 
     def quantize_f8(self, x: np.ndarray, H, L, D):

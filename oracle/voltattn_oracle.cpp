@@ -212,6 +212,64 @@ void or_quantize(const float* x, int H, int L, int D, int bits, uint8_t* codes, 
     }
 }
 
+// q4c+ quantizers (no reference counterpart): the group rule of or_quantize
+// with the group = one channel's L values of a head (K, scales [H][D]) or one
+// row's D values (V, scales [H][L]); codes packed as q8 / q4. bits = 8 or 4.
+static void put_code(uint8_t* codes, int bits, size_t e, int v) {
+    if (bits == 8) {
+        codes[e] = (uint8_t)(int8_t)v;
+    } else {
+        const uint8_t nib = (uint8_t)(v + 8);
+        uint8_t& b = codes[e / 2];
+        b = (e % 2 == 0) ? (uint8_t)((b & 0xF0) | nib) : (uint8_t)((b & 0x0F) | (nib << 4));
+    }
+}
+
+void or_quantize_kchan(const float* x, int H, int L, int D, int bits, uint8_t* codes, uint16_t* scales) {
+    const int lim = limit_for_bits(bits);
+    for (int h = 0; h < H; ++h)
+        for (int d = 0; d < D; ++d) {
+            float amax = 0.f;
+            for (int j = 0; j < L; ++j) amax = std::max(amax, std::fabs(x[((size_t)h * L + j) * D + d]));
+            const float s = amax > 0.f ? amax / (float)lim : 1.f;
+            scales[(size_t)h * D + d] = float_to_half_bits(s);
+            const float sh = half_bits_to_float(scales[(size_t)h * D + d]);
+            for (int j = 0; j < L; ++j) {
+                const size_t e = ((size_t)h * L + j) * D + d;
+                int v = (int)std::lrint(x[e] / sh);
+                put_code(codes, bits, e, std::max(-lim, std::min(lim, v)));
+            }
+        }
+}
+
+void or_quantize_vtok(const float* x, int H, int L, int D, int bits, uint8_t* codes, uint16_t* scales) {
+    const int lim = limit_for_bits(bits);
+    for (size_t r = 0; r < (size_t)H * L; ++r) {
+        float amax = 0.f;
+        for (int d = 0; d < D; ++d) amax = std::max(amax, std::fabs(x[r * D + d]));
+        const float s = amax > 0.f ? amax / (float)lim : 1.f;
+        scales[r] = float_to_half_bits(s);
+        const float sh = half_bits_to_float(scales[r]);
+        for (int d = 0; d < D; ++d) {
+            int v = (int)std::lrint(x[r * D + d] / sh);
+            put_code(codes, bits, r * D + d, std::max(-lim, std::min(lim, v)));
+        }
+    }
+}
+
+// Exact values float(double(scale) * code) of the two layouts.
+void or_dequant_kchan(const uint8_t* codes, const uint16_t* scales, int H, int L, int D, int bits, float* out) {
+    for (size_t idx = 0; idx < (size_t)H * L * D; ++idx) {
+        const size_t h = idx / ((size_t)L * D), d = idx % D;
+        out[idx] = (float)((double)half_bits_to_float(scales[h * D + d]) * code_at(codes, bits, idx));
+    }
+}
+
+void or_dequant_vtok(const uint8_t* codes, const uint16_t* scales, int H, int L, int D, int bits, float* out) {
+    for (size_t idx = 0; idx < (size_t)H * L * D; ++idx)
+        out[idx] = (float)((double)half_bits_to_float(scales[idx / D]) * code_at(codes, bits, idx));
+}
+
 // e4m3: round to nearest even, saturating to +-448; nan -> 0x7F.
 static uint8_t e4m3_encode(float x) {
     if (std::isnan(x)) return 0x7F;

@@ -59,7 +59,7 @@ def test_argument_errors_without_gpu():
     lib = va.lib()
     b = va.VaBufs(16, 16, 16, 16, 16, 16)
     ws, wb = C.c_void_p(256), 1 << 20
-    assert lib.va_decode(9, C.byref(b), 1, 1, 128, 1, ws, wb, None) == 1        # bad format
+    assert lib.va_decode(99, C.byref(b), 1, 1, 128, 1, ws, wb, None) == 1       # bad format
     assert lib.va_decode(1, C.byref(b), 1, 1, 96, 1, ws, wb, None) == 5         # D unsupported
     assert lib.va_decode(1, C.byref(b), 0, 1, 128, 1, ws, wb, None) == 1        # H < 1
     assert lib.va_decode(1, C.byref(b), 1, 0, 128, 1, ws, wb, None) == 1        # L < 1

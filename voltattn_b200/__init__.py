@@ -65,6 +65,9 @@ def _load():
     lib.va_exchange_combine.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
+    for fn in ("va_quantize_kchan", "va_quantize_vtok"):
+        getattr(lib, fn).argtypes = [i, vp, vp, vp, i, i, i, vp]
+        getattr(lib, fn).restype = i
     lib.va_decode_multiquery.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_multiquery.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
@@ -104,6 +107,7 @@ class Fmt(enum.IntEnum):
     Q3M = 6
     BF16M = 7  # bf16+ (no reference counterpart)
     F8M = 8    # f8+: e4m3 codes with fp16 group scales (no reference counterpart)
+    Q4CM = 9   # q4c+: q4 codes, K scales per (head, channel), V scales per row (no reference counterpart)
 
     @property
     def name_str(self) -> str:
@@ -122,7 +126,7 @@ class Fmt(enum.IntEnum):
 
 
 FORMATS = [Fmt(i) for i in range(7)]  # the reference's formats
-EXTRA_FORMATS = [Fmt.BF16M, Fmt.F8M]
+EXTRA_FORMATS = [Fmt.BF16M, Fmt.F8M, Fmt.Q4CM]
 
 
 def fmt_name(f) -> str:
@@ -135,7 +139,7 @@ def is_f16(f) -> bool:
 
 def qbits(f) -> int:
     """Quantization bits of a quantized format (src/voltattn.cu:691)."""
-    return {Fmt.Q8: 8, Fmt.Q8M: 8, Fmt.Q4: 4, Fmt.Q4M: 4, Fmt.Q3M: 3, Fmt.F8M: 8}.get(Fmt.parse(f), 8)
+    return {Fmt.Q8: 8, Fmt.Q8M: 8, Fmt.Q4: 4, Fmt.Q4M: 4, Fmt.Q3M: 3, Fmt.F8M: 8, Fmt.Q4CM: 4}.get(Fmt.parse(f), 8)
 
 
 def qbytes(bits: int, n: int) -> int:
@@ -248,6 +252,26 @@ def quantize_f8(x, H: int, L: int, D: int, codes=None, scales=None, stream=None)
     if scales is None:
         scales = torch.empty(H * L * (D // 64), dtype=torch.float16, device=x.device)
     _check(_lib.va_quantize_f8(_ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)), "quantize_f8")
+    return codes, scales
+
+
+def quantize_kchan(x, bits: int, H: int, L: int, D: int, stream=None):
+    """q4c+ K quantizer: scales per (head, channel) over all positions, [H][D]."""
+    import torch
+    codes = torch.empty(H * L * D * bits // 8, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(H * D, dtype=torch.float16, device=x.device)
+    _check(_lib.va_quantize_kchan(bits, _ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)),
+           "quantize_kchan")
+    return codes, scales
+
+
+def quantize_vtok(x, bits: int, H: int, L: int, D: int, stream=None):
+    """q4c+ V quantizer: one scale per row, [H][L]."""
+    import torch
+    codes = torch.empty(H * L * D * bits // 8, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(H * L, dtype=torch.float16, device=x.device)
+    _check(_lib.va_quantize_vtok(bits, _ptr(x), _ptr(codes), _ptr(scales), H, L, D, _stream_ptr(stream)),
+           "quantize_vtok")
     return codes, scales
 
 

@@ -57,17 +57,23 @@
 
 namespace va {
 
-template <Kind K, int D>
+// kChan: K codes with static per-channel scales per head ([H][D], folded into
+// the query once per unit) and V codes with one scale per row ([H][L]);
+// otherwise fp16 scales per 64-element group of every K and V row.
+template <Kind K, int D, bool kChanScales = false>
 struct TcCfg {
     static constexpr Kind kKind = K;
     static constexpr int kD = D;
     static constexpr int kG = 1;
+    static constexpr bool kChan = kChanScales;
     static constexpr int kBits = KindTraits<K>::kBits;
     static constexpr int kRb = D * kBits / 8;  // code bytes per row
     static constexpr int kChunks = kRb / 16;   // 16-byte chunks per row
     static constexpr int kPairs = kChunks / 2;
     static constexpr int kNgrp = D / kGroup;
-    static constexpr int kSb = 2 * kNgrp;  // scale bytes per row
+    static constexpr int kSbK = kChan ? 0 : 2 * kNgrp;  // K scale bytes per row
+    static constexpr int kSbV = kChan ? 2 : 2 * kNgrp;  // V scale bytes per row
+    static constexpr int kSb = kSbV;
     static constexpr int kWarps = 4;
     static constexpr int kRpw = 64;  // rows per warp per tile
     static constexpr int kTr = kWarps * kRpw;
@@ -75,10 +81,10 @@ struct TcCfg {
     static constexpr int kThreads = (kWarps + 2) * 32;  // consumers, producer, ticket warp
     static constexpr int kStages = 3;
     static constexpr int kTRing = 4;  // finished units handed to the ticket warp
-    static constexpr int kStageBytes = (2 * kTr * kRb + 2 * kTr * kSb + 1023) & ~1023;
+    static constexpr int kStageBytes = (2 * kTr * kRb + kTr * (kSbK + kSbV) + 1023) & ~1023;
     static constexpr int kPStage = 4 * 2 * 5 * 4 * 8;  // per warp: [block][group][slot][t'] 8-byte B fragments
     static constexpr int kMergeFloats = kWarps * (D + 2);
-    static constexpr int kQBytes = D * 2;  // one head's fp16 query, per stage
+    static constexpr int kQBytes = (kChan ? 2 : 1) * D * 2;  // the head's fp16 query (+ K channel scales)
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * 16 +
                                       kStages * kQBytes + kMergeFloats * 4 + kWarps * kPStage + 2 * kTRing * 8 +
                                       kTRing * 4 + 16 + 16 + kQBytes;
@@ -274,7 +280,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             uint8_t* sK = stages + (size_t)stage * C::kStageBytes;
             uint8_t* sV = sK + C::kTr * C::kRb;
             uint8_t* sSK = sV + C::kTr * C::kRb;
-            uint8_t* sSV = sSK + C::kTr * C::kSb;
+            uint8_t* sSV = sSK + C::kTr * C::kSbK;
             const long long t0 = tc_tile_row<C>(g, t);
             const long long tend = t0 + C::kTr;
             const int need = (int)(min(tend, r1b) - t0);
@@ -282,15 +288,33 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             const int brows = (int)max(0ll, min(tend, cend) - t0);
             const bool paged = p.page_rows > 0;
             const long long rg0 = max(t0, nr8), rg1 = min(tend, g.r1);
+            // a unit's first tile also carries the stream's query (and, with
+            // per-channel K scales, the head's channel scales right after it)
+            const uint32_t qb = t == 0 ? (uint32_t)C::kQBytes : 0u;
+            const auto copy_query = [&]() {
+                if constexpr (C::kChan) {
+                    bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kD, C::kD * 2, &full[stage], pol);
+                    bulk_g2s(qring + stage * C::kQBytes + C::kD * 2, p.scK + (size_t)g.h * C::kD, C::kD * 2,
+                             &full[stage], pol);
+                } else {  // the stream's kG query heads, contiguous
+                    bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage], pol);
+                }
+            };
             if (!paged && rg1 > rg0) {
                 // scales of the tensor's last partial 8-row block: plain loads
-                constexpr int kG = C::kSb / 2;
                 const int off = (int)(rg0 - t0);
                 const int rrows = (int)(rg1 - rg0);
-                for (int i = lane; i < rrows * kG; i += 32) {
-                    const int r = i / kG, w = i % kG;
-                    reinterpret_cast<__half*>(sSK)[(off + r) * kG + w] = p.scK[(size_t)(rg0 + r) * kG + w];
-                    reinterpret_cast<__half*>(sSV)[(off + r) * kG + w] = p.scV[(size_t)(rg0 + r) * kG + w];
+                if constexpr (C::kSbK > 0) {
+                    constexpr int kG = C::kSbK / 2;
+                    for (int i = lane; i < rrows * kG; i += 32) {
+                        const int r = i / kG, w = i % kG;
+                        reinterpret_cast<__half*>(sSK)[(off + r) * kG + w] = p.scK[(size_t)(rg0 + r) * kG + w];
+                    }
+                }
+                constexpr int kGv = C::kSbV / 2;
+                for (int i = lane; i < rrows * kGv; i += 32) {
+                    const int r = i / kGv, w = i % kGv;
+                    reinterpret_cast<__half*>(sSV)[(off + r) * kGv + w] = p.scV[(size_t)(rg0 + r) * kGv + w];
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -301,11 +325,9 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 for (int b = 0; b < C::kTr / C::kBox; ++b) ys[b] = __shfl_sync(0xffffffffu, py, b);
                 if (lane == 0) {
                     hdr[stage] = TcHeader{u, t, g.ntiles, 0};
-                    const uint32_t qb = t == 0 ? (uint32_t)C::kQBytes : 0u;
-                    mbar_arrive_expect_tx(&full[stage], (uint32_t)nbox * 2u * C::kBox * (C::kRb + C::kSb) + qb);
-                    if (qb)
-                        bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage],
-                                 pol);
+                    mbar_arrive_expect_tx(&full[stage],
+                                          (uint32_t)nbox * C::kBox * (2u * C::kRb + C::kSbK + C::kSbV) + qb);
+                    if (qb) copy_query();
                     int seg = 0;  // first box of the current run of physically contiguous boxes
 #pragma unroll
                     for (int b = 0; b < C::kTr / C::kBox; ++b) {
@@ -314,13 +336,14 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                         tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, ys[b], &full[stage], pol);
                         // scales: one bulk copy per run of contiguous boxes
                         if (b + 1 == nbox || ys[b + 1] != ys[b] + C::kBox) {
-                            const uint32_t nb = (uint32_t)(b + 1 - seg) * C::kBox * C::kSb;
-                            bulk_g2s(sSK + seg * C::kBox * C::kSb,
-                                     reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[seg] * C::kSb, nb,
-                                     &full[stage], pol);
-                            bulk_g2s(sSV + seg * C::kBox * C::kSb,
-                                     reinterpret_cast<const uint8_t*>(p.scV) + (size_t)ys[seg] * C::kSb, nb,
-                                     &full[stage], pol);
+                            const uint32_t rows = (uint32_t)(b + 1 - seg) * C::kBox;
+                            if constexpr (C::kSbK > 0)
+                                bulk_g2s(sSK + seg * C::kBox * C::kSbK,
+                                         reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[seg] * C::kSbK,
+                                         rows * C::kSbK, &full[stage], pol);
+                            bulk_g2s(sSV + seg * C::kBox * C::kSbV,
+                                     reinterpret_cast<const uint8_t*>(p.scV) + (size_t)ys[seg] * C::kSbV,
+                                     rows * C::kSbV, &full[stage], pol);
                             seg = b + 1;
                         }
                     }
@@ -330,22 +353,21 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             }
             if (lane == 0) {
                 hdr[stage] = TcHeader{u, t, g.ntiles, 0};
-                const uint32_t qb = t == 0 ? (uint32_t)C::kQBytes : 0u;
                 const uint32_t bytes =
-                    (uint32_t)nbox * 2u * C::kBox * C::kRb + (uint32_t)brows * 2u * C::kSb + qb;
+                    (uint32_t)nbox * 2u * C::kBox * C::kRb + (uint32_t)brows * (C::kSbK + C::kSbV) + qb;
                 mbar_arrive_expect_tx(&full[stage], bytes);
-                if (qb)  // the stream's kG query heads, contiguous
-                    bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage], pol);
+                if (qb) copy_query();
                 for (int b = 0; b < nbox; ++b) {
                     const int y = (int)(t0 + (long long)b * C::kBox);
                     tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, y, &full[stage], pol);
                     tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, y, &full[stage], pol);
                 }
                 if (brows > 0) {
-                    bulk_g2s(sSK, reinterpret_cast<const uint8_t*>(p.scK) + (size_t)t0 * C::kSb,
-                             (uint32_t)brows * C::kSb, &full[stage], pol);
-                    bulk_g2s(sSV, reinterpret_cast<const uint8_t*>(p.scV) + (size_t)t0 * C::kSb,
-                             (uint32_t)brows * C::kSb, &full[stage], pol);
+                    if constexpr (C::kSbK > 0)
+                        bulk_g2s(sSK, reinterpret_cast<const uint8_t*>(p.scK) + (size_t)t0 * C::kSbK,
+                                 (uint32_t)brows * C::kSbK, &full[stage], pol);
+                    bulk_g2s(sSV, reinterpret_cast<const uint8_t*>(p.scV) + (size_t)t0 * C::kSbV,
+                             (uint32_t)brows * C::kSbV, &full[stage], pol);
                 }
             }
             __syncwarp();
@@ -399,9 +421,22 @@ template <class C>
 __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int t, int lane) {
     constexpr int D = C::kD;
     static_assert(D == 128, "4 dims per lane");
+    static_assert(!C::kChan || C::kKind == Kind::Q4, "per-channel K scales: q4 codes");
     const uint2 w4 = reinterpret_cast<const uint2*>(qs)[lane];  // dims 4 lane .. 4 lane + 3
-    const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&w4.x));
-    const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&w4.y));
+    float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&w4.x));
+    float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&w4.y));
+    // per-channel K scales (stored after the query) fold into it: q'_d = q_d * s_d,
+    // exact in fp32 (a product of two fp16 values)
+    const __half* ks = qs + D;
+    if constexpr (C::kChan) {
+        const uint2 k4 = reinterpret_cast<const uint2*>(ks)[lane];
+        const float2 ka = __half22float2(*reinterpret_cast<const __half2*>(&k4.x));
+        const float2 kb = __half22float2(*reinterpret_cast<const __half2*>(&k4.y));
+        fa.x *= ka.x;
+        fa.y *= ka.y;
+        fb.x *= kb.x;
+        fb.y *= kb.y;
+    }
     float amax = fmaxf(fmaxf(fabsf(fa.x), fabsf(fa.y)), fmaxf(fabsf(fb.x), fabsf(fb.y)));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -421,10 +456,23 @@ __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int 
             for (int c = 0; c < 4; ++c) {  // 8 dims = 4 bytes per 16-byte load
                 const uint4 h = src[c];
                 const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+                uint32_t kw[4] = {0u, 0u, 0u, 0u};
+                if constexpr (C::kChan) {
+                    const uint4 hk = reinterpret_cast<const uint4*>(ks + 32 * t)[c];
+                    kw[0] = hk.x;
+                    kw[1] = hk.y;
+                    kw[2] = hk.z;
+                    kw[3] = hk.w;
+                }
                 uint32_t word = 0;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
+                    float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
+                    if constexpr (C::kChan) {
+                        const float2 fk = __half22float2(*reinterpret_cast<const __half2*>(&kw[j]));
+                        f.x *= fk.x;
+                        f.y *= fk.y;
+                    }
                     word |= tc_plane_byte(odd ? f.y : f.x, sc, plane) << (8 * j);
                 }
                 wl[c] = word;  // bytes 4c .. 4c+3 of the chunk
@@ -534,8 +582,13 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
         const int rbase = wrow + 16 * (2 * (t >> 1) + b);
-        f[b][0] = (float)u[b][0] * __half2float(sSK[(rbase + rowA) * C::kNgrp + grp]);
-        f[b][1] = (float)u[b][1] * __half2float(sSK[(rbase + rowB) * C::kNgrp + grp]);
+        if constexpr (C::kChan) {  // the K scales are in the query already
+            f[b][0] = (float)u[b][0];
+            f[b][1] = (float)u[b][1];
+        } else {
+            f[b][0] = (float)u[b][0] * __half2float(sSK[(rbase + rowA) * C::kNgrp + grp]);
+            f[b][1] = (float)u[b][1] * __half2float(sSK[(rbase + rowB) * C::kNgrp + grp]);
+        }
     }
     const int myrow0 = wrow + 16 * t + rowA, myrow1 = wrow + 16 * t + rowB;  // block t
     float s[2];
@@ -566,8 +619,15 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
     st.m = mnew;
     const float e0 = fast_exp2(s[0] - mnew), e1 = fast_exp2(s[1] - mnew);
     st.l = st.l * c + e0 + e1;
-    const float2 vs0 = __half22float2(*reinterpret_cast<const __half2*>(sSV + myrow0 * C::kNgrp));
-    const float2 vs1 = __half22float2(*reinterpret_cast<const __half2*>(sSV + myrow1 * C::kNgrp));
+    float2 vs0, vs1;
+    if constexpr (C::kChan) {  // one V scale per row, for both quant groups
+        const float a = __half2float(sSV[myrow0]), b = __half2float(sSV[myrow1]);
+        vs0 = make_float2(a, a);
+        vs1 = make_float2(b, b);
+    } else {
+        vs0 = __half22float2(*reinterpret_cast<const __half2*>(sSV + myrow0 * C::kNgrp));
+        vs1 = __half22float2(*reinterpret_cast<const __half2*>(sSV + myrow1 * C::kNgrp));
+    }
     float w[2][2] = {{e0 * vs0.x, e0 * vs0.y}, {e1 * vs1.x, e1 * vs1.y}};  // [row][group]
     if constexpr (kMasked) {
 #pragma unroll
@@ -828,7 +888,12 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             // the first unit's query goes out ahead of the tiles, so the
             // consumers prepare it while the tiles are in flight
             mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
-            bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
+            if constexpr (C::kChan) {
+                bulk_g2s(qfirst, p.q + (size_t)h0 * D, D * 2, qbar, l2_policy_evict_first());
+                bulk_g2s(qfirst + D * 2, p.scK + (size_t)h0 * D, D * 2, qbar, l2_policy_evict_first());
+            } else {
+                bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
+            }
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
@@ -913,7 +978,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             const long long t0 = tc_tile_row<C>(gm, h.tile);
             const uint32_t sK = smem_u32(base), sV = sK + C::kTr * C::kRb;
             const __half* sSK = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb);
-            const __half* sSV = sSK + C::kTr * C::kNgrp;
+            const __half* sSV = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb + C::kTr * C::kSbK);
             const long long w0 = t0 + wrow;
             const bool interior = w0 >= gm.r0 && w0 + C::kRpw <= gm.r1;
             if (interior)

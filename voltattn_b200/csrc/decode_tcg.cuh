@@ -43,6 +43,8 @@ struct TcgCfg {
     static constexpr int kChunks = kRb / 16;
     static constexpr int kNgrp = D / kGroup;
     static constexpr int kSb = 2 * kNgrp;
+    static constexpr bool kChan = false;  // group scales on every K and V row
+    static constexpr int kSbK = kSb, kSbV = kSb;
     static constexpr int kHg = G < 4 ? 1 : G / 4;  // head groups: 4 query head slots per consumer warp
     static constexpr int kRowWarps = 4;      // warps splitting a tile's rows
     static constexpr int kWarps = kRowWarps * kHg;

@@ -109,6 +109,77 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
                               grp, codes, scales);
 }
 
+// q4c+ (no reference counterpart, the layout of KIVI-style caches): K with a
+// static scale per (head, channel) over all positions, V with one scale per
+// row. Both follow the group rule above with the group being a channel's L
+// values (K) or a row's D values (V): s = amax > 0 ? amax / lim : 1 stored as
+// fp16, code = lrint(x / stored s) narrowed and clamped, packed as q8 / q4.
+
+// Per-channel K: CTA (head, 32-channel block), 256 threads = 32 channels x 8
+// row phases. Pass 1: channel amax over the head's L rows; pass 2: codes.
+template <int BITS>
+__global__ void __launch_bounds__(256) quantize_kchan_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
+                                                             __half* __restrict__ scales, int L, int D) {
+    constexpr int lim = BITS == 8 ? 127 : 7;
+    const int h = blockIdx.y, d = blockIdx.x * 32 + (threadIdx.x & 31), ph = threadIdx.x >> 5;
+    const float* xh = x + (size_t)h * L * D;
+    float amax = 0.f;
+    for (int j = ph; j < L; j += 8) amax = fmaxf(amax, fabsf(__ldg(xh + (size_t)j * D + d)));  // drops nan
+    __shared__ float red[8][32];
+    __shared__ float shs[32];
+    red[ph][threadIdx.x & 31] = amax;
+    __syncthreads();
+    if (ph == 0) {
+        for (int k = 1; k < 8; ++k) amax = fmaxf(amax, red[k][threadIdx.x & 31]);
+        const float sv = amax > 0.f ? __fdiv_rn(amax, (float)lim) : 1.f;
+        const __half hs = __float2half_rn(sv);
+        scales[(size_t)h * D + d] = hs;
+        shs[threadIdx.x & 31] = __half2float(hs);
+    }
+    __syncthreads();
+    const float sh = shs[threadIdx.x & 31];
+    for (int j = ph; j < L; j += 8) {
+        const int c = max(-lim, min(lim, lrint_narrow(__fdiv_rn(__ldg(xh + (size_t)j * D + d), sh))));
+        const size_t e = ((size_t)h * L + j) * D + d;
+        if constexpr (BITS == 8) {
+            codes[e] = (uint8_t)(int8_t)c;
+        } else {
+            // dims 2k (low nibble) and 2k+1 (high) of a byte: the even lane writes
+            const int hi = __shfl_down_sync(0xffffffffu, c, 1);
+            if ((d & 1) == 0) codes[e / 2] = (uint8_t)((c + 8) | ((hi + 8) << 4));
+        }
+    }
+}
+
+// Per-token V: one warp per row, D / 32 consecutive dims per lane.
+template <int BITS>
+__global__ void __launch_bounds__(256) quantize_vtok_kernel(const float* __restrict__ x, uint8_t* __restrict__ codes,
+                                                            __half* __restrict__ scales, long long rows, int D) {
+    constexpr int lim = BITS == 8 ? 127 : 7;
+    const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int per = D / 32;  // 4 (D = 128) or 2 (D = 64)
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < rows)
+        for (int i = 0; i < per; ++i) v[i] = __ldg(x + r * D + lane * per + i);
+    float amax = 0.f;
+    for (int i = 0; i < per; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (r >= rows) return;
+    const float sv = amax > 0.f ? __fdiv_rn(amax, (float)lim) : 1.f;
+    const __half hs = __float2half_rn(sv);
+    const float sh = __half2float(hs);
+    if (lane == 0) scales[r] = hs;
+    uint32_t w = 0;
+    for (int i = 0; i < per; ++i) {
+        const int c = max(-lim, min(lim, lrint_narrow(__fdiv_rn(v[i], sh))));
+        w |= BITS == 8 ? (uint32_t)(uint8_t)(int8_t)c << (8 * i) : (uint32_t)(c + 8) << (4 * i);
+    }
+    uint8_t* dst = codes + (size_t)r * D * BITS / 8 + (size_t)lane * per * BITS / 8;
+    for (int i = 0; i < per * BITS / 8; ++i) dst[i] = (uint8_t)(w >> (8 * i));
+}
+
 // KV append: new rows x [B*Hkv][D] (one token per sequence) quantized into a
 // cache [B][Hkv][Lcap][D] at row pos[b] of every KV head of sequence b, with
 // the same arithmetic as quantize_kernel (the rows come out exactly as if the

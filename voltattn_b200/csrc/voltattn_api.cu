@@ -38,11 +38,11 @@ int cuda_fail(cudaError_t e) {
         if (e__ != cudaSuccess) return cuda_fail(e__);  \
     } while (0)
 
-bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_F8P; }
+bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_Q4CP; }
 bool is_f16(int f) { return f == VA_F16 || f == VA_F16P || f == VA_BF16P; }  // 16-bit rows, no scales
 bool is_plain(int f) { return f == VA_F16 || f == VA_Q8 || f == VA_Q4; }
 int fmt_bits(int f) {
-    return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P || f == VA_F8P) ? 8 : (f == VA_Q3P) ? 3 : 4;
+    return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P || f == VA_F8P) ? 8 : (f == VA_Q3P) ? 3 : 4;  // q4c+: 4
 }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -461,6 +461,16 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
     if (partial && !fused_ok) return VA_ERR_WORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* slots = static_cast<float*>(ws);
+    if (fmt == VA_Q4CP) {  // tile kernel only: D = 128, fused workspace, bulk-copied query
+        if (D != 128) return VA_ERR_UNSUPPORTED;
+        if (!fused_ok) return VA_ERR_WORKSPACE;
+        if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;
+        if ((long long)H * L >= (1ll << 31)) return VA_ERR_TOO_LARGE;
+        unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
+        const DecodeParams p =
+            make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+        return launch_tc<TcCfg<Kind::Q4, 128, true>>(p, st);
+    }
     if (is_plain(fmt) || !fused_ok) {
         if (is_plain(fmt)) {
             if (partial) return VA_ERR_UNSUPPORTED;
@@ -510,13 +520,13 @@ extern "C" {
 int va_version(void) { return 100; }
 
 const char* va_fmt_name(int fmt) {
-    static const char* names[] = {"f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+", "bf16+", "f8+"};
+    static const char* names[] = {"f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+", "bf16+", "f8+", "q4c+"};
     return is_valid_fmt(fmt) ? names[fmt] : nullptr;
 }
 
 int va_fmt_from_name(const char* name) {
     if (!name) return -1;
-    for (int f = VA_F16; f <= VA_F8P; ++f)
+    for (int f = VA_F16; f <= VA_Q4CP; ++f)
         if (std::strcmp(name, va_fmt_name(f)) == 0) return f;
     return -1;
 }
@@ -575,7 +585,11 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
     double unit_rows;  // fixed cost of a unit in rows of streaming
     const bool tc = D == 128 && (fmt == VA_Q4P || fmt == VA_Q8P) &&
                     pick_consumer(fmt == VA_Q4P ? Kind::Q4 : Kind::Q8, D, 1) == Consumer::kTc;
-    if (tc) {
+    if (fmt == VA_Q4CP) {
+        rc = tc_ctas_per_sm<TcCfg<Kind::Q4, 128, true>>(dev, &occ);
+        tr = TcCfg<Kind::Q4, 128, true>::kTr;
+        unit_rows = 512.0;
+    } else if (tc) {
         // tile kernel: per-unit query setup, slot and ticket hand-over
         rc = fmt == VA_Q4P ? tc_ctas_per_sm<TcCfg<Kind::Q4, 128>>(dev, &occ)
                            : tc_ctas_per_sm<TcCfg<Kind::Q8, 128>>(dev, &occ);
@@ -677,6 +691,35 @@ int va_quantize_f8(const float* x, void* codes, void* scales, int H, int L, int 
     const unsigned blocks = (unsigned)((ngroups * 8 + 255) / 256);
     quantize_kernel<kBitsF8><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         x, static_cast<uint8_t*>(codes), static_cast<__half*>(scales), ngroups);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+int va_quantize_kchan(int bits, const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {
+    if ((bits != 8 && bits != 4) || !x || !codes || !scales || H < 1 || L < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(scales) & 1u)) return VA_ERR_ALIGN;
+    const dim3 grid((unsigned)(D / 32), (unsigned)H);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* c = static_cast<uint8_t*>(codes);
+    auto* sc = static_cast<__half*>(scales);
+    if (bits == 8) quantize_kchan_kernel<8><<<grid, 256, 0, st>>>(x, c, sc, L, D);
+    else quantize_kchan_kernel<4><<<grid, 256, 0, st>>>(x, c, sc, L, D);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
+int va_quantize_vtok(int bits, const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {
+    if ((bits != 8 && bits != 4) || !x || !codes || !scales || H < 1 || L < 1) return VA_ERR_INVALID;
+    if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(scales) & 1u)) return VA_ERR_ALIGN;
+    const long long rows = (long long)H * L;
+    const unsigned blocks = (unsigned)((rows + 7) / 8);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* c = static_cast<uint8_t*>(codes);
+    auto* sc = static_cast<__half*>(scales);
+    if (bits == 8) quantize_vtok_kernel<8><<<blocks, 256, 0, st>>>(x, c, sc, rows, D);
+    else quantize_vtok_kernel<4><<<blocks, 256, 0, st>>>(x, c, sc, rows, D);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }
