@@ -191,6 +191,13 @@ VA_API int va_quantize_kchan(int bits, const float* x, void* codes, void* scales
 VA_API int va_quantize_vtok(int bits, const float* x, void* codes, void* scales, int H, int L, int D,
                             void* stream);
 
+/* Copies `bytes` (a multiple of 16; both pointers 16-byte aligned) with a small
+ * kernel of loads and stores. Either pointer may be pinned host memory
+ * (cudaHostAlloc / cudaMallocHost: mapped into the device address space under
+ * unified addressing), which moves a decode step's query in and its output
+ * out without a copy-engine transfer (no reference counterpart). */
+VA_API int va_copy_small(void* dst, const void* src, size_t bytes, void* stream);
+
 /* KV append for decode loops (no reference counterpart; the reference
  * quantizes a whole cache once). Quantizes one new row per KV head of each
  * sequence, x = fp32 [B][Hkv][D], into a cache laid out as for

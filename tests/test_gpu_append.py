@@ -90,3 +90,19 @@ def test_append_then_decode_loop(va, oracle):
         got = out.float().cpu().numpy()
         err = np.abs(got - ref)
         assert (err <= 2e-3 + 1e-3 * np.abs(ref)).all(), (step, float(err.max()))
+
+
+def test_copy_small_pinned_and_device(va):
+    """va_copy_small between device memory and device-mapped pinned host memory."""
+    import torch
+    src = torch.randn(4096).half().pin_memory()
+    dev = torch.empty(4096, dtype=torch.float16, device="cuda")
+    back = torch.empty(4096, dtype=torch.float16).pin_memory()
+    va.copy_small(dev, src)
+    va.copy_small(back, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(back, src)
+    d2 = torch.empty_like(dev)
+    va.copy_small(d2, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(d2, dev)

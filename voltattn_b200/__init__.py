@@ -65,6 +65,7 @@ def _load():
     lib.va_exchange_combine.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
+    lib.va_copy_small.argtypes = [vp, vp, sz, vp]; lib.va_copy_small.restype = i
     for fn in ("va_quantize_kchan", "va_quantize_vtok"):
         getattr(lib, fn).argtypes = [i, vp, vp, vp, i, i, i, vp]
         getattr(lib, fn).restype = i
@@ -241,6 +242,14 @@ def append_kv(x, bits: int, codes, scales, B: int, Hkv: int, Lcap: int, D: int, 
     with quantize() of the whole cache. bits 16 stores fp16 rows."""
     _check(_lib.va_append_kv(bits, _ptr(x), _ptr(codes), _ptr(scales), B, Hkv, Lcap, D, _ptr(pos),
                              _stream_ptr(stream)), "append_kv")
+
+
+def copy_small(dst, src, stream=None):
+    """Copy between two same-size tensors by a small kernel; either may be pinned
+    host memory (device-mapped under unified addressing)."""
+    nbytes = src.numel() * src.element_size()
+    assert dst.numel() * dst.element_size() == nbytes
+    _check(_lib.va_copy_small(_ptr(dst), _ptr(src), nbytes, _stream_ptr(stream)), "copy_small")
 
 
 def quantize_f8(x, H: int, L: int, D: int, codes=None, scales=None, stream=None):

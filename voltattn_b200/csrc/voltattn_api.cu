@@ -682,6 +682,29 @@ int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int 
     return VA_OK;
 }
 
+namespace {
+// Small transfers by loads and stores (16-byte words, grid-stride). Either side
+// may be pinned host memory, which unified addressing maps into the device's
+// address space: a few KB then cost a kernel instead of a copy-engine transfer.
+__global__ void __launch_bounds__(256) copy_small_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                         size_t n16) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+}  // namespace
+
+int va_copy_small(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!dst || !src) return VA_ERR_INVALID;
+    if (!aligned16(dst) || !aligned16(src) || (bytes & 15u)) return VA_ERR_ALIGN;
+    if (bytes == 0) return VA_OK;
+    const size_t n16 = bytes / 16;
+    const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 1184);
+    copy_small_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint4*>(dst),
+                                                                            static_cast<const uint4*>(src), n16);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
 int va_quantize_f8(const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {
     if (!x || !codes || !scales || H < 1 || L < 1) return VA_ERR_INVALID;
     if (D != 64 && D != 128) return VA_ERR_UNSUPPORTED;
