@@ -230,8 +230,9 @@ VA_API int va_decode_multiquery(int fmt, const va_bufs* bufs, const int* lens, i
  * (device int32 [B][max_pages]) at row j % page_rows. lens: device int32 [B],
  * 1 <= lens[b] <= max_pages * page_rows. Entries outside [0, num_pages) read
  * page 0 (decode) or skip the row (append). Supported: D = 128, page_rows a
- * multiple of 32, q4+ / q8+ with Hq == Hkv and q4+ with Hq == 4 * Hkv (the
- * tensor-core tile kernels); other shapes return VA_ERR_UNSUPPORTED. q must be
+ * multiple of 32, q3+ / q4+ / q8+ with Hq == Hkv and q4+ with Hq == 2, 4 or
+ * 8 * Hkv (the tensor-core tile kernels); other shapes return
+ * VA_ERR_UNSUPPORTED. q must be
  * 16-byte aligned. ws as for va_decode_gqa (va_gqa_workspace_bytes). Splits
  * s of a sequence take its 256-row tiles s, s + S, s + 2S, ... */
 VA_API int va_decode_paged(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, const int* lens,

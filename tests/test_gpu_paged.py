@@ -66,6 +66,8 @@ CASES = [  # fmt, B, Hq, Hkv, Lmax, page_rows, S
     ("q4+", 1, 32, 8, 4100, 128, 4),
     ("q4+", 2, 16, 2, 900, 64, 2),   # 8 query heads per KV head
     ("q4+", 2, 8, 4, 500, 32, 2),    # 2 query heads per KV head
+    ("q3+", 3, 4, 4, 777, 96, 3),
+    ("q3+", 2, 2, 2, 1500, 32, 4),
 ]
 
 
@@ -149,5 +151,5 @@ def test_paged_rejects_unsupported(va):
     b = va.DeviceBufs(K, K, sK, sK, q, out, ws)
     with pytest.raises(RuntimeError):  # page rows not a multiple of 32
         va.decode_paged("q4+", b, bt, max_pages, lens, B, Hq, Hkv, page_rows, num_pages, D, 1)
-    with pytest.raises(RuntimeError):  # q3+ has no paged kernel
-        va.decode_paged("q3+", b, bt, max_pages, lens, B, Hq, Hkv, 32, num_pages, D, 1)
+    with pytest.raises(RuntimeError):  # q3+ pages: one query head per KV head only
+        va.decode_paged("q3+", b, bt, max_pages, lens, B, 2 * Hq, Hkv, 32, num_pages, D, 1)

@@ -67,8 +67,14 @@ struct TcCfg {
     static constexpr int kG = 1;
     static constexpr bool kChan = kChanScales;
     static constexpr int kBits = KindTraits<K>::kBits;
-    static constexpr int kRb = D * kBits / 8;  // code bytes per row
-    static constexpr int kChunks = kRb / 16;   // 16-byte chunks per row
+    // q3 and q4 codes both run the two-field-per-byte path (kNib): q4 bytes
+    // hold two nibbles, q3 granules are widened to two 3-bit fields per byte
+    static constexpr bool kNib = K == Kind::Q4 || K == Kind::Q3;
+    static constexpr int kRb = D * kBits / 8;  // code bytes per row (global rows, stages)
+    // bytes per row of the swizzled compute tile: the stage itself, or for q3
+    // the per-warp V buffer of widened rows (K is widened in registers)
+    static constexpr int kRbT = K == Kind::Q3 ? D / 2 : kRb;
+    static constexpr int kChunks = kRbT / 16;  // 16-byte chunks per compute row
     static constexpr int kPairs = kChunks / 2;
     static constexpr int kNgrp = D / kGroup;
     static constexpr int kSbK = kChan ? 0 : 2 * kNgrp;  // K scale bytes per row
@@ -87,16 +93,19 @@ struct TcCfg {
     static constexpr int kPStage = 4 * 2 * 5 * 4 * 8;  // per warp: [block][group][slot][t'] 8-byte B fragments
     static constexpr int kMergeFloats = kWarps * (D + 2);
     static constexpr int kQBytes = (kChan ? 2 : 1) * D * 2;  // the head's fp16 query (+ K channel scales)
-    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * 16 +
+    static constexpr int kVBuf = K == Kind::Q3 ? kWarps * kRpw * kRbT : 0;  // q3: widened V rows per warp
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kVBuf + 2 * kStages * 8 + kStages * 16 +
                                       kStages * kQBytes + kMergeFloats * 4 + kWarps * kPStage + 2 * kTRing * 8 +
                                       kTRing * 4 + 16 + 16 + kQBytes;
-    static_assert(K == Kind::Q4 || K == Kind::Q8, "integer 4- and 8-bit codes");
+    static_assert(K == Kind::Q3 || K == Kind::Q4 || K == Kind::Q8, "integer 3-, 4- and 8-bit codes");
     static_assert(D == 128, "two quant groups per row");
-    static_assert(kRb == 64 || kRb == 128, "swizzle span = row");
+    static_assert(kRbT == 64 || kRbT == 128, "swizzle span = row");
+    static_assert(K != Kind::Q3 || !kChan, "q3 codes: per-group scales");
     static_assert(kMergeFloats >= kWarps * 32 + 64, "merge area doubles as combine scratch");
     static_assert(kTr % kBox == 0 && kBox % 8 == 0, "whole boxes of 8-row blocks");
     // 16-byte alignment of the bulk-copy targets carved after the stages
-    static_assert((kStages * kStageBytes + 2 * kStages * 8 + kStages * 16) % 16 == 0, "query ring");
+    static_assert((kStages * kStageBytes + kVBuf + 2 * kStages * 8 + kStages * 16) % 16 == 0, "query ring");
+    static_assert(kVBuf % 1024 == 0, "stage alignment after the V buffers");
     static_assert((kStages * kQBytes + kMergeFloats * 4 + kWarps * kPStage + 2 * kTRing * 8 + kTRing * 4 + 16) %
                       16 == 0,
                   "first-unit query");
@@ -109,7 +118,7 @@ struct TcCfg {
 // (the swizzle period).
 template <class C>
 __host__ __device__ constexpr int tc_row_a(int q) {
-    return C::kKind == Kind::Q4 ? q : ((q >> 1) | ((q & 1) << 2));
+    return C::kKind != Kind::Q8 ? q : ((q >> 1) | ((q & 1) << 2));
 }
 template <class C>
 __host__ __device__ constexpr int tc_row_b(int q) {
@@ -123,8 +132,40 @@ __host__ __device__ constexpr int tc_q1(int tp) { return 4 * (tp & 1) + (tp >> 1
 // 1024-byte aligned: chunk bits 4.. XOR offset bits 7.. (span = row bytes).
 template <class C>
 __host__ __device__ constexpr int tc_swz(int row, int chunk) {
-    return row * C::kRb + 16 * (chunk ^ ((row * C::kRb >> 7) & (C::kRb / 16 - 1)));
+    return row * C::kRbT + 16 * (chunk ^ ((row * C::kRbT >> 7) & (C::kRbT / 16 - 1)));
 }
+
+// One 12-byte q3 granule (32 fields, field i at bits 3i..3i+2 of the
+// little-endian stream) widened to the 16-byte chunk layout of q4: byte b
+// holds fields 2b (bits 0..2) and 2b+1 (bits 3..5), so raw & 7 is the even
+// field and raw - (raw & 7) = 8 * the odd field. Per 24-bit segment (bits
+// above 24 are ignored): 12-bit halves to 16-bit halves, 6-bit pairs to
+// bytes, each a shift and a bit select that leaves stray bits only in bits
+// 6..7 of the bytes, then one mask clears those.
+__device__ __forceinline__ uint32_t tc_widen_q3_seg(uint32_t s) {
+    const uint32_t x = (s & 0x0000FFFFu) | ((s << 4) & 0xFFFF0000u);
+    const uint32_t y = (x & 0x00FF00FFu) | ((x << 2) & 0xFF00FF00u);
+    return y & 0x3F3F3F3Fu;
+}
+__device__ __forceinline__ uint4 tc_widen_q3(uint32_t w0, uint32_t w1, uint32_t w2) {
+    uint4 r;
+    r.x = tc_widen_q3_seg(w0);                         // stream bits 0..23
+    r.y = tc_widen_q3_seg(__funnelshift_r(w0, w1, 24));  // 24..47
+    r.z = tc_widen_q3_seg(__funnelshift_r(w1, w2, 16));  // 48..71
+    r.w = tc_widen_q3_seg(w2 >> 8);                    // 72..95
+    return r;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 
 // ---- PTX wrappers -----------------------------------------------------------------
 
@@ -216,6 +257,10 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
     const int lane = threadIdx.x & 31;
     const uint64_t pol = l2_policy_evict_first();
     const long long nr8 = p.total_rows & ~7ll;
+    // q3 rows (48 bytes) are copied as flat byte ranges: a tensor copy issues
+    // one request per row, and 48-byte rows straddle 32-byte sectors (about
+    // twice the L2 requests of the data, measured)
+    constexpr bool kFlatRows = C::kKind == Kind::Q3;
     const int nunits = p.H * p.S;
     unsigned* sched = p.counters + p.H;
     // First unit: blockIdx.x. Later units come from the counter (offset by
@@ -334,11 +379,19 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
 #pragma unroll
                     for (int b = 0; b < C::kTr / C::kBox; ++b) {
                         if (b >= nbox) break;
-                        tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, ys[b], &full[stage], pol);
-                        tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, ys[b], &full[stage], pol);
-                        // scales: one bulk copy per run of contiguous boxes
+                        if constexpr (!kFlatRows) {
+                            tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, ys[b], &full[stage], pol);
+                            tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, ys[b], &full[stage], pol);
+                        }
+                        // scales (and flat codes): one bulk copy per run of contiguous boxes
                         if (b + 1 == nbox || ys[b + 1] != ys[b] + C::kBox) {
                             const uint32_t rows = (uint32_t)(b + 1 - seg) * C::kBox;
+                            if constexpr (kFlatRows) {
+                                bulk_g2s(sK + seg * C::kBox * C::kRb, p.K + (size_t)ys[seg] * C::kRb,
+                                         rows * C::kRb, &full[stage], pol);
+                                bulk_g2s(sV + seg * C::kBox * C::kRb, p.V + (size_t)ys[seg] * C::kRb,
+                                         rows * C::kRb, &full[stage], pol);
+                            }
                             if constexpr (C::kSbK > 0)
                                 bulk_g2s(sSK + seg * C::kBox * C::kSbK,
                                          reinterpret_cast<const uint8_t*>(p.scK) + (size_t)ys[seg] * C::kSbK,
@@ -355,14 +408,25 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             }
             if (lane == 0) {
                 hdr[stage] = TcHeader{u, t, g.ntiles, 0};
-                const uint32_t bytes =
-                    (uint32_t)nbox * 2u * C::kBox * C::kRb + (uint32_t)brows * (C::kSbK + C::kSbV) + qb;
+                // flat codes: the tile's rows inside the tensor, one bulk copy
+                // per matrix (rows past the end stay stale; they are masked)
+                const uint32_t crows =
+                    kFlatRows ? (uint32_t)max(0ll, min((long long)nbox * C::kBox, p.total_rows - t0))
+                              : (uint32_t)nbox * C::kBox;
+                const uint32_t bytes = crows * 2u * C::kRb + (uint32_t)brows * (C::kSbK + C::kSbV) + qb;
                 mbar_arrive_expect_tx(&full[stage], bytes);
                 if (qb) copy_query();
-                for (int b = 0; b < nbox; ++b) {
-                    const int y = (int)(t0 + (long long)b * C::kBox);
-                    tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, y, &full[stage], pol);
-                    tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, y, &full[stage], pol);
+                if constexpr (kFlatRows) {
+                    if (crows > 0) {
+                        bulk_g2s(sK, p.K + (size_t)t0 * C::kRb, crows * C::kRb, &full[stage], pol);
+                        bulk_g2s(sV, p.V + (size_t)t0 * C::kRb, crows * C::kRb, &full[stage], pol);
+                    }
+                } else {
+                    for (int b = 0; b < nbox; ++b) {
+                        const int y = (int)(t0 + (long long)b * C::kBox);
+                        tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, y, &full[stage], pol);
+                        tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, y, &full[stage], pol);
+                    }
                 }
                 if (brows > 0) {
                     if constexpr (C::kSbK > 0)
@@ -447,7 +511,7 @@ __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int 
     const int e = amax > 0.f ? 14 - (((__float_as_int(amax) >> 23) & 0xFF) - 126) : 0;
     const float sc = __int_as_float((127 + e) << 23);
     const int n = g, plane = g & 1;
-    if constexpr (C::kKind == Kind::Q4) {
+    if constexpr (C::kNib) {
         const bool active = ((n >> 1) & 1) == (t >> 1);
         const int odd = n >= 4 ? 1 : 0;
         // dims 32 t .. 32 t + 31 of this lane's chunk: byte b holds dims 2b, 2b+1
@@ -495,7 +559,8 @@ __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int 
 #pragma unroll
         for (int off = 1; off < 16; off <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);  // lanes of a group
         const int s0 = __shfl_sync(0xffffffffu, sq, 0), s1 = __shfl_sync(0xffffffffu, sq, 16);
-        tq.bias = t == 0 ? -8 * s0 : t == 1 ? -8 * s1 : 0;
+        constexpr int kZero = C::kKind == Kind::Q3 ? 4 : 8;  // code of value 0
+        tq.bias = t == 0 ? -kZero * s0 : t == 1 ? -kZero * s1 : 0;
     } else {
         const int ia = 2 * ((n >> 1) & 1) + (n >> 2);  // the mma whose column pair holds n
         const int chunk = t + 4 * (ia >> 1);
@@ -517,7 +582,8 @@ __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int 
         tq.bias = 0;
     }
     const float base = rsqrtf((float)D) * kLog2e;
-    tq.qs = base / sc * (C::kKind == Kind::Q4 ? 0.0625f : 1.f);
+    // the two-field path scores 16 (q4) or 8 (q3) times the dot product
+    tq.qs = base / sc * (C::kKind == Kind::Q4 ? 0.0625f : C::kKind == Kind::Q3 ? 0.125f : 1.f);
 }
 
 // ---- one tile of one warp ------------------------------------------------------------------
@@ -525,17 +591,50 @@ __device__ __forceinline__ void tc_load_q(TcQ& tq, const __half* qs, int g, int 
 template <class C>
 struct TcState {
     float m, l;
-    float o[C::kPairs][C::kKind == Kind::Q4 ? 4 : 2];
+    float o[C::kPairs][C::kNib ? 4 : 2];
 };
 
 template <class C, bool kMasked>
 __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* sSK, const __half* sSV, uint8_t* sp,
                                         int wrow, int g, int t, long long t0, long long r0, long long r1,
-                                        const TcQ& tq, const uint32_t* voff, TcState<C>& st) {
-    constexpr bool kQ4 = C::kKind == Kind::Q4;
+                                        const TcQ& tq, const uint32_t* voff, uint32_t vbuf, TcState<C>& st) {
+    constexpr bool kQ4 = C::kNib;  // q4 and (widened) q3: two fields per byte
+    constexpr bool kQ3 = C::kKind == Kind::Q3;
     constexpr int kRb = C::kRb;
+    // low field mask and the factor between the high field and raw - low
+    constexpr uint32_t m4 = kQ3 ? 0x07070707u : 0x0F0F0F0Fu;
+    constexpr int kHiMul = kQ3 ? 8 : 16;
+    constexpr int kZero = kQ3 ? 4 : 8;  // code of value 0
     const int rowA = tc_row_a<C>(g), rowB = tc_row_b<C>(g);
     const uint32_t offA = (uint32_t)tc_swz<C>(rowA, t), offB = (uint32_t)tc_swz<C>(rowB, t);
+    if constexpr (kQ3) {
+        // widen this warp's 64 V rows into its buffer in the q4 chunk layout
+        // (lane: granule lane % 4 of rows lane / 4 + 8 i), read back below by
+        // ldmatrix; the previous tile's reads of the buffer are done (the
+        // __syncwarp that ends tc_tile). All loads first: the shared-memory
+        // accesses are volatile, so they issue in program order.
+        const int r0_ = (threadIdx.x & 31) / 4, c = threadIdx.x & 3;
+        uint32_t raw[8][3];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) raw[i][k] = lds32(sV + (uint32_t)((wrow + r0_ + 8 * i) * kRb + 12 * c + 4 * k));
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            sts128(vbuf + (uint32_t)tc_swz<C>(r0_ + 8 * i, c), tc_widen_q3(raw[i][0], raw[i][1], raw[i][2]));
+    }
+    // q3: granule t of rows A and B of every block, loaded ahead of the mmas
+    uint32_t kraw[kQ3 ? 4 : 1][2][3];
+    if constexpr (kQ3) {
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const uint32_t rb = sK + (uint32_t)((wrow + 16 * blk) * kRb + 12 * t + 4 * k);
+                kraw[blk][0][k] = lds32(rb + (uint32_t)(rowA * kRb));
+                kraw[blk][1][k] = lds32(rb + (uint32_t)(rowB * kRb));
+            }
+    }
 
     // ---- scores: lane partials per block, rows A and B ------------------------------------
     int v[4][2];
@@ -543,15 +642,21 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
     for (int blk = 0; blk < 4; ++blk) {
         const uint32_t rb = sK + (uint32_t)((wrow + 16 * blk) * kRb);
         if constexpr (kQ4) {
-            const uint4 wa = lds128(rb + offA), wb = lds128(rb + offB);
-            const uint32_t m4 = 0x0F0F0F0Fu;
+            uint4 wa, wb;
+            if constexpr (kQ3) {  // granule t of rows A and B, widened in registers
+                wa = tc_widen_q3(kraw[blk][0][0], kraw[blk][0][1], kraw[blk][0][2]);
+                wb = tc_widen_q3(kraw[blk][1][0], kraw[blk][1][1], kraw[blk][1][2]);
+            } else {
+                wa = lds128(rb + offA);
+                wb = lds128(rb + offB);
+            }
             int a1[4] = {0, tq.bias, 0, tq.bias}, a2[4] = {0, 0, 0, 0};
             mma_k32<false, true>(a1, wa.x & m4, wb.x & m4, wa.y & m4, wb.y & m4, tq.b[0][0], tq.b[0][1]);
             mma_k32<false, true>(a1, wa.z & m4, wb.z & m4, wa.w & m4, wb.w & m4, tq.b[1][0], tq.b[1][1]);
             mma_k32<false, true>(a2, wa.x, wb.x, wa.y, wb.y, tq.b[2][0], tq.b[2][1]);
             mma_k32<false, true>(a2, wa.z, wb.z, wa.w, wb.w, tq.b[3][0], tq.b[3][1]);
-            // lanes t < 2: 16 * (low nibbles . even q); t >= 2: raw . odd q - low . odd q
-            const int alpha = t < 2 ? 16 : -1;
+            // lanes t < 2: 16 (8) * (low fields . even q); t >= 2: raw . odd q - low . odd q
+            const int alpha = t < 2 ? kHiMul : -1;
             v[blk][0] = alpha * (256 * a1[0] + a1[1]) + (256 * a2[0] + a2[1]);
             v[blk][1] = alpha * (256 * a1[2] + a1[3]) + (256 * a2[2] + a2[3]);
         } else {
@@ -677,6 +782,9 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
             for (int x = 0; x < (kQ4 ? 4 : 2); ++x) st.o[pi][x] *= c;
     }
     const int slot = min(g, 4);
+    // V tile: the stage (q4, q8) or the warp's widened rows (q3)
+    const uint32_t vrows = kQ3 ? vbuf : sV + (uint32_t)(wrow * C::kRbT);
+    if constexpr (kQ3) __syncwarp();  // the widened rows are visible to the warp
     if constexpr (kQ4) {
         // two accumulator sets (blocks 0,1 and 2,3): shorter mma dependency chains
         int aR[2][2][4], aL[2][2][4];
@@ -685,17 +793,16 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 aL[c][pi][0] = aL[c][pi][2] = 0;
-                aL[c][pi][1] = aL[c][pi][3] = c == 0 ? -8 * psum[pi] : 0;
+                aL[c][pi][1] = aL[c][pi][3] = c == 0 ? -kZero * psum[pi] : 0;
                 aR[c][pi][0] = aR[c][pi][2] = 0;
-                aR[c][pi][1] = aR[c][pi][3] = c == 0 ? -136 * psum[pi] : 0;
+                aR[c][pi][1] = aR[c][pi][3] = c == 0 ? -(kZero + kHiMul * kZero) * psum[pi] : 0;
             }
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
 #pragma unroll
             for (int pi = 0; pi < 2; ++pi) {
                 const uint2 bf = *reinterpret_cast<const uint2*>(sp + ((blk * 2 + pi) * 5 + slot) * 32 + t * 8);
-                const uint4 a = ldsm_x2_trans_b8(sV + (uint32_t)((wrow + 16 * blk) * kRb) + voff[pi]);
-                const uint32_t m4 = 0x0F0F0F0Fu;
+                const uint4 a = ldsm_x2_trans_b8(vrows + (uint32_t)(16 * blk * C::kRbT) + voff[pi]);
                 mma_k32<false, false>(aR[blk >> 1][pi], a.x, a.y, a.z, a.w, bf.x, bf.y);
                 mma_k32<false, false>(aL[blk >> 1][pi], a.x & m4, a.y & m4, a.z & m4, a.w & m4, bf.x, bf.y);
             }
@@ -705,7 +812,7 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
             const auto sum = [&](int (&a)[2][2][4], int x) { return a[0][pi][x] + a[1][pi][x]; };
             const int xl0 = 256 * sum(aL, 0) + sum(aL, 1), xl1 = 256 * sum(aL, 2) + sum(aL, 3);
             const int xr0 = 256 * sum(aR, 0) + sum(aR, 1), xr1 = 256 * sum(aR, 2) + sum(aR, 3);
-            const float ws = wscale[pi], ws16 = wscale[pi] * 0.0625f;
+            const float ws = wscale[pi], ws16 = wscale[pi] * (1.f / kHiMul);
             st.o[pi][0] = fmaf((float)xl0, ws, st.o[pi][0]);
             st.o[pi][1] = fmaf((float)(xr0 - xl0), ws16, st.o[pi][1]);
             st.o[pi][2] = fmaf((float)xl1, ws, st.o[pi][2]);
@@ -725,7 +832,7 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
                 bf[gi] = *reinterpret_cast<const uint2*>(sp + ((blk * 2 + gi) * 5 + slot) * 32 + t * 8);
 #pragma unroll
             for (int pi = 0; pi < C::kPairs; ++pi) {
-                const uint4 a = ldsm_x2_trans_b8(sV + (uint32_t)((wrow + 16 * blk) * kRb) + voff[pi]);
+                const uint4 a = ldsm_x2_trans_b8(vrows + (uint32_t)(16 * blk * C::kRbT) + voff[pi]);
                 const uint2 b = bf[pi / (C::kPairs / 2)];
                 mma_k32<true, false>(acc[pi], a.x, a.y, a.z, a.w, b.x, b.y);
             }
@@ -744,7 +851,7 @@ __device__ __forceinline__ void tc_tile(uint32_t sK, uint32_t sV, const __half* 
 template <class C>
 __device__ __forceinline__ int tc_out_dim(int pi, int x, int g, int t) {
     const int chunk = 2 * pi + t;
-    if constexpr (C::kKind == Kind::Q4) return 2 * (16 * chunk + g + 8 * (x >> 1)) + (x & 1);
+    if constexpr (C::kNib) return 2 * (16 * chunk + g + 8 * (x >> 1)) + (x & 1);
     else return 16 * chunk + g + 8 * x;
 }
 
@@ -847,7 +954,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     extern __shared__ __align__(128) uint8_t smem_raw[];
     constexpr int D = C::kD;
     uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(stages + C::kStages * C::kStageBytes);
+    uint8_t* vbufs = stages + C::kStages * C::kStageBytes;  // q3: per-warp widened V rows
+    uint64_t* full = reinterpret_cast<uint64_t*>(vbufs + C::kVBuf);
     uint64_t* empty = full + C::kStages;
     TcHeader* hdr = reinterpret_cast<TcHeader*>(empty + C::kStages);
     uint8_t* qring = reinterpret_cast<uint8_t*>(hdr + C::kStages);
@@ -911,6 +1019,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     const int g = lane >> 2, t = lane & 3, tid = threadIdx.x;
     uint8_t* sp = shP + warp * C::kPStage;
     const int wrow = warp * C::kRpw;
+    const uint32_t vbuf = smem_u32(vbufs) + (uint32_t)(warp * C::kRpw * C::kRbT);
     // ldmatrix row addresses of this lane (k = lane & 15 of chunk 2 pi + lane / 16)
     uint32_t voff[C::kPairs];
     {
@@ -974,7 +1083,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
 #pragma unroll
             for (int pi = 0; pi < C::kPairs; ++pi)
 #pragma unroll
-                for (int x = 0; x < (C::kKind == Kind::Q4 ? 4 : 2); ++x) st.o[pi][x] = 0.f;
+                for (int x = 0; x < (C::kNib ? 4 : 2); ++x) st.o[pi][x] = 0.f;
         }
         if (h.ntiles > 0) {
             const long long t0 = tc_tile_row<C>(gm, h.tile);
@@ -984,9 +1093,9 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             const long long w0 = t0 + wrow;
             const bool interior = w0 >= gm.r0 && w0 + C::kRpw <= gm.r1;
             if (interior)
-                tc_tile<C, false>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, st);
+                tc_tile<C, false>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, vbuf, st);
             else
-                tc_tile<C, true>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, st);
+                tc_tile<C, true>(sK, sV, sSK, sSV, sp, wrow, g, t, t0, gm.r0, gm.r1, tq, voff, vbuf, st);
         }
         if (lane == 0) mbar_arrive(&empty[stage]);
         if (h.tile < h.ntiles - 1) continue;
@@ -999,7 +1108,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
 #pragma unroll
             for (int pi = 0; pi < C::kPairs; ++pi)
 #pragma unroll
-                for (int x = 0; x < (C::kKind == Kind::Q4 ? 4 : 2); ++x)
+                for (int x = 0; x < (C::kNib ? 4 : 2); ++x)
                     shMerge[warp * D + tc_out_dim<C>(pi, x, g, t)] = st.o[pi][x];
         }
         if (lane == 0) {

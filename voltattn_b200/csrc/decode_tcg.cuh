@@ -40,6 +40,7 @@ struct TcgCfg {
     static constexpr int kG = G;
     static constexpr int kBits = KindTraits<K>::kBits;
     static constexpr int kRb = D * kBits / 8;
+    static constexpr int kRbT = kRb;  // compute-tile row bytes (the swizzle span)
     static constexpr int kChunks = kRb / 16;
     static constexpr int kNgrp = D / kGroup;
     static constexpr int kSb = 2 * kNgrp;

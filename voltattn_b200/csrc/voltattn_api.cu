@@ -105,7 +105,8 @@ Consumer pick_consumer(Kind k, int D, int G) {
         return -1;
     }();
     const bool tc_ok =
-        D == 128 && ((G == 1 && (k == Kind::Q4 || k == Kind::Q8)) || ((G == 2 || G == 4 || G == 8) && k == Kind::Q4));
+        D == 128 && ((G == 1 && (k == Kind::Q3 || k == Kind::Q4 || k == Kind::Q8)) ||
+                     ((G == 2 || G == 4 || G == 8) && k == Kind::Q4));
     if (v == 0) return Consumer::kDp;
     if (v == 1) return Consumer::kMma;
     if (v == 2 && tc_ok) return Consumer::kTc;
@@ -170,7 +171,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // [rows][row_bytes] uint8 codes, boxes of box_rows full rows, swizzle span =
-// row bytes (64 or 128), zero fill past the last row.
+// row bytes (64 or 128; other widths, the 48-byte q3 rows, unswizzled), zero
+// fill past the last row.
 int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int row_bytes, int box_rows) {
     const auto enc = tensor_map_encoder();
     if (!enc) return VA_ERR_UNSUPPORTED;
@@ -178,7 +180,9 @@ int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int row_by
     const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
     const cuuint32_t box[2] = {(cuuint32_t)row_bytes, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                    : CU_TENSOR_MAP_SWIZZLE_NONE;
     const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -283,7 +287,8 @@ template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
     if constexpr (!is_float_kind(C::kKind)) {
         const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
-        if constexpr (C::kG == 1 && C::kD == 128 && (C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
+        if constexpr (C::kG == 1 && C::kD == 128 &&
+                      (C::kKind == Kind::Q3 || C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
             // tensor coordinates are 32-bit
             // and the query is bulk-copied
             if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
@@ -583,17 +588,19 @@ int va_suggest_splits(int fmt, int H, int L, int D, int* S) {
     int occ = 1;
     int tr;
     double unit_rows;  // fixed cost of a unit in rows of streaming
-    const bool tc = D == 128 && (fmt == VA_Q4P || fmt == VA_Q8P) &&
-                    pick_consumer(fmt == VA_Q4P ? Kind::Q4 : Kind::Q8, D, 1) == Consumer::kTc;
+    const Kind kk = fmt == VA_Q4P ? Kind::Q4 : fmt == VA_Q8P ? Kind::Q8 : Kind::Q3;
+    const bool tc = D == 128 && (fmt == VA_Q4P || fmt == VA_Q8P || fmt == VA_Q3P) &&
+                    pick_consumer(kk, D, 1) == Consumer::kTc;
     if (fmt == VA_Q4CP) {
         rc = tc_ctas_per_sm<TcCfg<Kind::Q4, 128, true>>(dev, &occ);
         tr = TcCfg<Kind::Q4, 128, true>::kTr;
         unit_rows = 512.0;
     } else if (tc) {
         // tile kernel: per-unit query setup, slot and ticket hand-over
-        rc = fmt == VA_Q4P ? tc_ctas_per_sm<TcCfg<Kind::Q4, 128>>(dev, &occ)
-                           : tc_ctas_per_sm<TcCfg<Kind::Q8, 128>>(dev, &occ);
-        tr = fmt == VA_Q4P ? TcCfg<Kind::Q4, 128>::kTr : TcCfg<Kind::Q8, 128>::kTr;
+        rc = fmt == VA_Q4P   ? tc_ctas_per_sm<TcCfg<Kind::Q4, 128>>(dev, &occ)
+             : fmt == VA_Q8P ? tc_ctas_per_sm<TcCfg<Kind::Q8, 128>>(dev, &occ)
+                             : tc_ctas_per_sm<TcCfg<Kind::Q3, 128>>(dev, &occ);
+        tr = TcCfg<Kind::Q4, 128>::kTr;  // 256 rows for every format
         unit_rows = 512.0;
     } else {
         rc = stream_cfg_occupancy(fmt, D, dev, &occ);
@@ -908,11 +915,13 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || max_pages < 1 || page_rows < 1 || num_pages < 1 || S < 1)
         return VA_ERR_INVALID;
     const int G = Hq / Hkv;
-    // the tile kernels: q4+ / q8+ batch-1 layout (G = 1), q4+ with G = 4; copy
-    // boxes of 32 rows stay inside a page
+    // the tile kernels: q3+ / q4+ / q8+ with one query head per KV head, q4+
+    // with 2, 4 or 8; copy boxes of 32 rows stay inside a page
+    const Kind kind = fmt == VA_Q8P ? Kind::Q8 : fmt == VA_Q3P ? Kind::Q3 : Kind::Q4;
     const bool ok = D == 128 && page_rows % 32 == 0 &&
-                    ((G == 1 && (fmt == VA_Q4P || fmt == VA_Q8P)) || ((G == 2 || G == 4 || G == 8) && fmt == VA_Q4P)) &&
-                    pick_consumer(fmt == VA_Q8P ? Kind::Q8 : Kind::Q4, D, G) == Consumer::kTc;
+                    ((G == 1 && (fmt == VA_Q3P || fmt == VA_Q4P || fmt == VA_Q8P)) ||
+                     ((G == 2 || G == 4 || G == 8) && fmt == VA_Q4P)) &&
+                    pick_consumer(kind, D, G) == Consumer::kTc;
     if (!ok) return VA_ERR_UNSUPPORTED;
     const long long streams = (long long)B * Hkv;
     const long long rows = (long long)num_pages * Hkv * page_rows;
@@ -936,6 +945,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     if (G == 2) return launch_tcg<TcgCfg<Kind::Q4, 128, 2>>(p, st);
     if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
     if (G == 8) return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
+    if (fmt == VA_Q3P) return launch_tc<TcCfg<Kind::Q3, 128>>(p, st);
     return fmt == VA_Q4P ? launch_tc<TcCfg<Kind::Q4, 128>>(p, st) : launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
 }
 
