@@ -1,0 +1,94 @@
+"""Prefill (va_prefill): Lq new tokens of one sequence, causal over the cache
+whose last Lq rows are theirs, on the tcgen05 tensor cores. Checked against the
+oracle's GQA restatement of the reference's per-head math
+(src/voltattn.cu:769-794) run once per token with the token's visible length
+L - Lq + 1 + i. No reference counterpart (the reference decodes one token)."""
+import numpy as np
+import pytest
+
+from oracle.oracle import BITS
+
+pytestmark = pytest.mark.gpu
+
+# K and V are rounded to fp16 tile by tile (code * scale) and P is fp16 in the
+# tensor-core product: the same bar as the decode kernels
+ATOL, RTOL = 2e-3, 1e-3
+
+
+@pytest.fixture(scope="module")
+def va():
+    import torch
+    assert torch.cuda.is_available()
+    import voltattn_b200
+    return voltattn_b200
+
+
+CASES = [  # fmt, Hq, Hkv, L, Lq
+    ("q4+", 8, 2, 700, 300),   # 4 query heads per KV head, tokens not a multiple of 128
+    ("q8+", 4, 4, 256, 256),   # the whole cache is new
+    ("f16+", 2, 1, 1000, 130),
+    ("q3+", 4, 2, 500, 129),
+    ("q4", 4, 4, 128, 1),      # one token: a decode
+    ("f16", 2, 2, 333, 77),
+    ("q8", 2, 1, 1500, 200),
+    ("q4+", 2, 2, 2049, 640),  # several token blocks, cache blocks past the diagonal
+]
+
+
+def cache_for(oracle, fmt, kx, vx, rows, D):
+    """Device-side codes and scales plus the exact values the reference attends over."""
+    if fmt.startswith("f16"):
+        kb, vb = oracle.f2h(kx), oracle.f2h(vx)
+        return kb, vb, None, None, oracle.round_to_half(kx), oracle.round_to_half(vx)
+    bits = BITS[fmt]
+    kc, ks = oracle.quantize(kx, 1, rows, D, bits)
+    vc, vs = oracle.quantize(vx, 1, rows, D, bits)
+    return kc, vc, ks, vs, oracle.dequant(kc, ks, 1, rows, D, bits), oracle.dequant(vc, vs, 1, rows, D, bits)
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "{}_Hq{}_Hkv{}_L{}_Lq{}".format(*c))
+def test_prefill(va, oracle, case):
+    import torch
+    fmt, Hq, Hkv, L, Lq = case
+    D = 128
+    rng = np.random.default_rng(Hq * 131 + Hkv * 17 + L + Lq)
+    rows = Hkv * L
+    kx, vx, _ = oracle.gen_case(int(rng.integers(1 << 30)), 1, rows, D)
+    kc, vc, ks, vs, kd, vd = cache_for(oracle, fmt, kx, vx, rows, D)
+    q = oracle.f2h(rng.standard_normal(Hq * Lq * D).astype(np.float32)).reshape(Hq, Lq, D)
+    ref = np.empty((Hq, Lq, D), np.float32)
+    for i in range(Lq):
+        li = np.array([L - Lq + 1 + i], np.int32)
+        ref[:, i] = oracle.reference_gqa(kd, vd, np.ascontiguousarray(q[:, i]).ravel(), li, 1, Hq, Hkv, L,
+                                         D).reshape(Hq, D)
+    dev = "cuda"
+    as_dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    K, V = as_dev(kc), as_dev(vc)
+    sK = None if ks is None else as_dev(ks).view(torch.float16)
+    sV = None if vs is None else as_dev(vs).view(torch.float16)
+    qd = as_dev(q.ravel()).view(torch.float16)
+    out = torch.full((Hq * Lq * D,), float("nan"), dtype=torch.float16, device=dev)
+    b = va.DeviceBufs(K, V, sK, sV, qd, out)
+    for _ in range(2):
+        va.prefill(fmt, b, Hq, Hkv, L, Lq, D)
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy().reshape(Hq, Lq, D)
+        err = np.abs(got - ref)
+        bad = ~(err <= ATOL + RTOL * np.abs(ref))
+        assert not bad.any(), f"{case}: {bad.sum()} bad, maxerr {np.nanmax(err):.3e}"
+    assert va.device_error() == 0
+
+
+def test_prefill_rejects_unsupported(va):
+    import torch
+    Hq, Hkv, L, Lq = 2, 2, 64, 8
+    K = torch.zeros(Hkv * L * 64, dtype=torch.uint8, device="cuda")
+    s = torch.zeros(Hkv * L * 2, dtype=torch.float16, device="cuda")
+    q = torch.zeros(Hq * Lq * 64, dtype=torch.float16, device="cuda")
+    b = va.DeviceBufs(K, K, s, s, q, q.clone())
+    with pytest.raises(RuntimeError):  # D = 64
+        va.prefill("q4+", b, Hq, Hkv, L, Lq, 64)
+    with pytest.raises(RuntimeError):  # more new tokens than cache rows
+        va.prefill("q4+", b, Hq, Hkv, 4, Lq, 128)
+    with pytest.raises(RuntimeError):  # bf16+ has no prefill
+        va.prefill("bf16+", b, Hq, Hkv, L, Lq, 128)

@@ -71,6 +71,8 @@ def _load():
         getattr(lib, fn).restype = i
     lib.va_decode_multiquery.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_multiquery.restype = i
+    lib.va_prefill.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, i, vp]
+    lib.va_prefill.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_paged.restype = i
     lib.va_append_kv_paged.argtypes = [i, vp, vp, vp, vp, i, i, i, i, i, i, vp, vp]
@@ -300,6 +302,15 @@ def decode_multiquery(fmt, b: DeviceBufs, lens, B: int, Hq: int, Hkv: int, Q: in
     _check(_lib.va_decode_multiquery(int(Fmt.parse(fmt)), C.byref(vb), _ptr(lens), B, Hq, Hkv, Q, Lmax, D, S,
                                      _ptr(b.ws), b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)),
            "decode_multiquery")
+
+
+def prefill(fmt, b: DeviceBufs, Hq: int, Hkv: int, L: int, Lq: int, D: int, stream=None):
+    """Attention of the Lq new tokens of one sequence over its cache (the
+    tokens' rows are its last Lq rows; token i sees rows [0, L - Lq + i]) on
+    the tcgen05 tensor cores. b.K / b.V: [Hkv][L] rows; b.q, b.out: fp16
+    [Hq][Lq][D]; b.ws unused."""
+    vb = b.va()
+    _check(_lib.va_prefill(int(Fmt.parse(fmt)), C.byref(vb), Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill")
 
 
 def decode_paged(fmt, b: DeviceBufs, block_table, max_pages: int, lens, B: int, Hq: int, Hkv: int, page_rows: int,

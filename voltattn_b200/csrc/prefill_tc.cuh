@@ -1,0 +1,377 @@
+// Prefill (multi-token) attention over the quantized KV cache on the
+// Blackwell tensor cores: tcgen05.mma with shared-memory operands and
+// accumulators in tensor memory (TMEM).
+//
+// The reference decodes one token at a time and has no prefill (its README
+// lists batch-1 single-token decode as a limitation); the math per query row
+// is the reference's (src/voltattn.cu:769-794): score_j = q.K_j / sqrt(D),
+// softmax over the visible rows, o = sum_j p_j V_j, with K_j, V_j the
+// dequantized cache rows (src/voltattn.cu:747-767: code * fp16 scale).
+//
+// Problem: Lq new tokens of one sequence whose K/V rows are already in the
+// cache as its last Lq rows, Hq query heads over Hkv KV heads (head h reads
+// KV head h / (Hq / Hkv)). Token i (0-based) sees cache rows
+// [0, L - Lq + i] (causal). q, out: fp16 [Hq][Lq][D]; cache [Hkv][L] rows.
+//
+// One CTA per (query head, block of 128 tokens), 8 warps, 1 CTA per SM.
+// Per block of 128 cache rows:
+//   1. all warps dequantize the block's K and V rows to fp16 into shared
+//      memory (plain loads; code * scale rounded to fp16);
+//   2. one thread issues S = Q K^T as 8 tcgen05.mma (M = 128 tokens,
+//      N = 128 rows, K = 16 dims each) into TMEM columns [0, 128);
+//   3. warps 0..3 (TMEM lanes 0..127, one token row per thread) read S,
+//      mask, run the online softmax in registers, write P (fp16) to shared
+//      memory and rescale the running O in TMEM when the row maximum moved;
+//   4. one thread issues O += P V as 8 tcgen05.mma (N = 128 dims, K = 16
+//      rows each) into TMEM columns [128, 256).
+// The tiles use the canonical 128-byte-swizzled layout: two 64-element
+// panels of 128 rows, row r of a panel at r * 128 bytes, 16-byte chunk c at
+// (c ^ (r & 7)) * 16. The K tile is read K-major (rows = N), the V tile,
+// with the same bytes layout, MN-major (dims contiguous), so V needs no
+// transpose. Every wait on an mbarrier is bounded.
+#pragma once
+
+#include "common.cuh"
+#include "formats.cuh"
+
+namespace va {
+
+struct PrefillParams {
+    const uint8_t* K;
+    const uint8_t* V;
+    const __half* scK;
+    const __half* scV;
+    const __half* q;
+    __half* out;
+    int Hq, Hkv, L, Lq;
+};
+
+template <Kind K>
+struct PrefillCfg {
+    static constexpr Kind kKind = K;
+    static constexpr int kD = 128;
+    static constexpr int kBq = 128;  // tokens per CTA (MMA M)
+    static constexpr int kBk = 128;  // cache rows per block (MMA N of S, K of O)
+    static constexpr int kThreads = 256;
+    static constexpr int kRb = kD * KindTraits<K>::kBits / 8;  // code bytes per cache row
+    static constexpr int kTile = kBq * kD * 2;                 // one fp16 128 x 128 tile
+    static constexpr int kSmemBytes = 1024 + 4 * kTile + 64;   // Q, K, V, P + barriers
+    static constexpr int kTmemCols = 256;                      // S and O, 128 fp32 columns each
+    static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
+};
+
+// ---- tcgen05 / TMEM wrappers (PTX ISA 8.6+, sm_100a) ---------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc05_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc05_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: start, leading and stride byte offsets
+// (16-byte units, 14 bits each), descriptor version 1 (bits 46..47), layout
+// 128-byte swizzle (value 2 in bits 61..63).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator (bits 4..5 = 1), fp16
+// A and B (formats 0), A K-major, B K-major or MN-major (bit 16), N >> 3 in
+// bits 17..22, M >> 4 in bits 24..28.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool b_mn_major) {
+    return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+// Arrives on the mbarrier once all tcgen05.mma issued so far by this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp w of a
+// warpgroup reads lanes 32 w .. 32 w + 31). The wait is in the same asm
+// statement, so no use of the outputs can be scheduled before it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Byte offset of (row, 16-byte chunk 0..15) in a swizzled 128 x 128 fp16 tile.
+__host__ __device__ constexpr uint32_t pf_off(int row, int chunk) {
+    return (uint32_t)((chunk >> 3) * 16384 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+// Dims 8 c .. 8 c + 7 of cache row `row` (global), dequantized to fp16.
+template <Kind K>
+__device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half* scales, long long row, int c) {
+    constexpr int kRb = PrefillCfg<K>::kRb;
+    const uint8_t* src = codes + (size_t)row * kRb;
+    if constexpr (K == Kind::F16) {
+        return __ldg(reinterpret_cast<const uint4*>(src) + c);
+    } else {
+        const float s = __half2float(__ldg(scales + (size_t)row * 2 + (c >> 3)));
+        float v[8];
+        if constexpr (K == Kind::Q8) {
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(src) + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[i] = (float)(int8_t)(w.x >> (8 * i));
+                v[4 + i] = (float)(int8_t)(w.y >> (8 * i));
+            }
+        } else if constexpr (K == Kind::Q4) {
+            // byte b of the chunk holds dims 2b (low nibble) and 2b+1; nibble = code + 8
+            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src) + c);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = (float)((int)((w >> (4 * i)) & 0xFu) - 8);
+        } else {
+            // dims 8c .. 8c+7: bits 24c .. 24c+23 of the row, field = code + 4
+            const uint32_t x = (uint32_t)__ldg(src + 3 * c) | ((uint32_t)__ldg(src + 3 * c + 1) << 8) |
+                               ((uint32_t)__ldg(src + 3 * c + 2) << 16);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = (float)((int)((x >> (3 * i)) & 7u) - 4);
+        }
+        uint4 r;
+        uint32_t* rw = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h = __floats2half2_rn(v[2 * i] * s, v[2 * i + 1] * s);
+            rw[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        return r;
+    }
+}
+
+__device__ __forceinline__ void sts128_generic(uint8_t* base, uint32_t off, uint4 v) {
+    *reinterpret_cast<uint4*>(base + off) = v;
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1) prefill_tc_kernel(const PrefillParams p) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* sQ = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sK = sQ + C::kTile;
+    uint8_t* sV = sK + C::kTile;
+    uint8_t* sP = sV + C::kTile;
+    uint64_t* bar_s = reinterpret_cast<uint64_t*>(sP + C::kTile);
+    uint64_t* bar_o = bar_s + 1;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
+    volatile int* fail = reinterpret_cast<volatile int*>(tslot + 1);
+
+    constexpr int D = C::kD;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nqb = (int)gridDim.x;
+    const int qb = nqb - 1 - (int)blockIdx.x;  // the longest (last) token blocks start first
+    const int h = (int)blockIdx.y;
+    const int hk = h / (p.Hq / p.Hkv);
+    const int q0 = qb * C::kBq;
+    const long long off0 = (long long)p.L - p.Lq;  // cache row of token 0
+
+    if (warp == 0) tmem_alloc(tslot, C::kTmemCols);
+    if (tid == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        *fail = 0;
+        fence_mbar_init();
+    }
+    // this CTA's query tokens -> sQ (rows past Lq are zero)
+    for (int i = tid; i < C::kBq * 16; i += C::kThreads) {
+        const int r = i >> 4, c = i & 15;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (q0 + r < p.Lq)
+            v = __ldg(reinterpret_cast<const uint4*>(p.q + ((size_t)h * p.Lq + q0 + r) * D) + c);
+        sts128_generic(sQ, pf_off(r, c), v);
+    }
+    tc05_fence_before();
+    __syncthreads();
+    tc05_fence_after();
+    const uint32_t tbase = *tslot;
+    const uint32_t tS = tbase, tO = tbase + 128;
+    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV), sPa = smem_u32(sP);
+    constexpr uint32_t kIdescS = umma_idesc_f16(128, 128, false);
+    constexpr uint32_t kIdescO = umma_idesc_f16(128, 128, true);
+
+    // cache rows this CTA needs: [0, last], last = min(L - 1, off0 + q0 + 127)
+    const long long last = min((long long)p.L - 1, off0 + q0 + C::kBq - 1);
+    const int nkb = (int)(last / C::kBk) + 1;
+    const bool softmax_warp = warp < 4;
+    const int row = tid;  // token row of softmax threads (TMEM lane)
+    const long long vis = off0 + q0 + row;  // last visible cache row of this token
+    const float qk_scale = rsqrtf((float)D) * kLog2e;
+    float m = kNegMax, l = 0.f;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+
+    for (int kb = 0; kb < nkb; ++kb) {
+        const long long r0 = (long long)kb * C::kBk;
+        // 1. dequantize the block's K and V rows (rows past L: zero, masked)
+        for (int i = tid; i < C::kBk * 16; i += C::kThreads) {
+            const int r = i >> 4, c = i & 15;
+            const long long gr = r0 + r;
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+            if (gr < p.L) {
+                const long long grow = (long long)hk * p.L + gr;
+                kv = pf_dequant8<C::kKind>(p.K, p.scK, grow, c);
+                vv = pf_dequant8<C::kKind>(p.V, p.scV, grow, c);
+            }
+            sts128_generic(sK, pf_off(r, c), kv);
+            sts128_generic(sV, pf_off(r, c), vv);
+        }
+        fence_proxy_async_smem();
+        tc05_fence_before();
+        __syncthreads();
+        // 2. S = Q K^T
+        if (tid == 0) {
+            tc05_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t o = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                umma_f16(tS, umma_desc_sw128(sQa + o, 16, 1024), umma_desc_sw128(sKa + o, 16, 1024), kIdescS,
+                         kk > 0);
+            }
+            umma_commit(bar_s);
+        }
+        const bool ok_s = mbar_wait_bounded(bar_s, (uint32_t)kb & 1u);
+        if (!ok_s && lane == 0) report_error(kErrFullWait);
+        tc05_fence_after();
+        if (__syncthreads_or(!ok_s)) {  // every thread leaves together
+            if (tid == 0) *fail = 1;
+            break;
+        }
+        // 3. online softmax of this thread's token row; P -> sP; rescale O
+        if (softmax_warp) {
+            float s[C::kBk];
+#pragma unroll
+            for (int cb = 0; cb < C::kBk / 32; ++cb) tmem_ld32(tS + lane_addr + 32 * cb, s + 32 * cb);
+            float bm = kNegMax;
+#pragma unroll
+            for (int j = 0; j < C::kBk; ++j) {
+                const bool ok = r0 + j <= vis && r0 + j < p.L;
+                s[j] = ok ? s[j] * qk_scale : -INFINITY;
+                bm = fmaxf(bm, s[j]);
+            }
+            const float mnew = fmaxf(m, bm);
+            const float corr = fast_exp2(m - mnew);
+            m = mnew;
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float a = fast_exp2(s[8 * c + 2 * i] - mnew), b = fast_exp2(s[8 * c + 2 * i + 1] - mnew);
+                    sum += a + b;
+                    const __half2 hp = __floats2half2_rn(a, b);
+                    w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                }
+                sts128_generic(sP, pf_off(row, c), make_uint4(w[0], w[1], w[2], w[3]));
+            }
+            l = l * corr + sum;
+            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    float o[32];
+                    tmem_ld32(tO + lane_addr + 32 * cb, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    tmem_st32(tO + lane_addr + 32 * cb, o);
+                }
+                tmem_wait_st();
+            }
+        }
+        fence_proxy_async_smem();
+        tc05_fence_before();
+        __syncthreads();
+        // 4. O += P V
+        if (tid == 0) {
+            tc05_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < C::kBk / 16; ++kk) {
+                const uint32_t oa = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                const uint32_t ob = (uint32_t)(kk * 16 * 128);  // 16 cache rows of 128 bytes per panel
+                umma_f16(tO, umma_desc_sw128(sPa + oa, 16, 1024), umma_desc_sw128(sVa + ob, 16384, 1024), kIdescO,
+                         kb > 0 || kk > 0);
+            }
+            umma_commit(bar_o);
+        }
+        const bool ok_o = mbar_wait_bounded(bar_o, (uint32_t)kb & 1u);
+        if (!ok_o && lane == 0) report_error(kErrFullWait);
+        tc05_fence_after();
+        if (__syncthreads_or(!ok_o)) {
+            if (tid == 0) *fail = 1;
+            break;
+        }
+    }
+    // epilogue: out = O / l for the CTA's valid tokens
+    __syncthreads();
+    if (softmax_warp && !*fail) {
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+            float o[32];
+            tmem_ld32(tO + lane_addr + 32 * cb, o);
+            if (q0 + row < p.Lq) {
+                uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)h * p.Lq + q0 + row) * D + 32 * cb);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __half2 hp = __floats2half2_rn(o[8 * c + 2 * i] * inv, o[8 * c + 2 * i + 1] * inv);
+                        w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                    }
+                    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+    }
+    tc05_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc05_fence_after();
+        tmem_dealloc(tbase, C::kTmemCols);
+    }
+}
+
+}  // namespace va

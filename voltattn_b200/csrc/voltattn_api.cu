@@ -18,6 +18,7 @@
 #include "decode_tc.cuh"
 #include "decode_tcg.cuh"
 #include "exchange.cuh"
+#include "prefill_tc.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
 
@@ -520,6 +521,27 @@ int noalloc_scratch(int dev, void** out) {
 
 }  // namespace
 
+template <class C>
+int launch_prefill(const PrefillParams& p, cudaStream_t st) {
+    int dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    static bool attr_set[kMaxDevices] = {false};
+    static std::mutex mu;
+    if (!attr_set[dev]) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attr_set[dev]) {
+            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            attr_set[dev] = true;
+        }
+    }
+    const dim3 grid((unsigned)((p.Lq + C::kBq - 1) / C::kBq), (unsigned)p.Hq);
+    prefill_tc_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
+    VA_CUDA(cudaGetLastError());
+    return VA_OK;
+}
+
 extern "C" {
 
 int va_version(void) { return 100; }
@@ -992,6 +1014,37 @@ int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, 
     VA_CUDA(cudaMemsetAsync(base + counters_offset(H, D, S), 0, need - counters_offset(H, D, S),
                             static_cast<cudaStream_t>(stream)));
     return decode_impl(fmt, bufs, H, L, D, S, ws, need, nullptr, stream);
+}
+
+int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* stream) {
+    if (!is_valid_fmt(fmt) || !b) return VA_ERR_INVALID;
+    if (Hq < 1 || Hkv < 1 || Hq % Hkv || Lq < 1 || L < Lq) return VA_ERR_INVALID;
+    if (D != 128) return VA_ERR_UNSUPPORTED;
+    if (fmt == VA_BF16P || fmt == VA_F8P || fmt == VA_Q4CP) return VA_ERR_UNSUPPORTED;
+    if (Hq > 65535 || (long long)Hkv * L >= (1ll << 40)) return VA_ERR_TOO_LARGE;
+    if (!b->K || !b->V || !b->q || !b->out) return VA_ERR_INVALID;
+    if (!is_f16(fmt) && (!b->scK || !b->scV)) return VA_ERR_INVALID;
+    if (!aligned16(b->K) || !aligned16(b->V) || !aligned16(b->q) || !aligned16(b->out)) return VA_ERR_ALIGN;
+    if (!is_f16(fmt) && ((reinterpret_cast<uintptr_t>(b->scK) & 3u) || (reinterpret_cast<uintptr_t>(b->scV) & 3u)))
+        return VA_ERR_ALIGN;
+    PrefillParams p;
+    p.K = static_cast<const uint8_t*>(b->K);
+    p.V = static_cast<const uint8_t*>(b->V);
+    p.scK = static_cast<const __half*>(b->scK);
+    p.scV = static_cast<const __half*>(b->scV);
+    p.q = static_cast<const __half*>(b->q);
+    p.out = static_cast<__half*>(b->out);
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.L = L;
+    p.Lq = Lq;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (fmt_bits(fmt)) {
+        case 16: return launch_prefill<PrefillCfg<Kind::F16>>(p, st);
+        case 8: return launch_prefill<PrefillCfg<Kind::Q8>>(p, st);
+        case 4: return launch_prefill<PrefillCfg<Kind::Q4>>(p, st);
+        default: return launch_prefill<PrefillCfg<Kind::Q3>>(p, st);
+    }
 }
 
 int va_device_error(int* code) {
