@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
+    ap.add_argument("--prefill-lq", type=int, default=0,
+                    help="with --profile: prefill of this many tokens (cache of --L rows, 32/8 heads) instead")
     ap.add_argument("--gqa-batch", type=int, default=0,
                     help="with --profile: the batched GQA decode of config 5 with this many sequences instead")
     return ap.parse_args()
@@ -519,6 +521,63 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
             "steps": n, "launches_per_step": 1}
 
 
+def make_prefill(va, torch, dev, fmt, Hq, Hkv, L, Lq, seed):
+    """One sequence's cache of L rows per KV head (its last Lq rows are the new
+    tokens) in format fmt, quantized on the GPU, and the tokens' fp16 queries."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    rows = Hkv * L
+    bits = FORMAT_BITS[fmt]
+    kx = torch.randn(rows * D, device=dev, generator=g)
+    vx = torch.randn(rows * D, device=dev, generator=g)
+    if bits == 16:
+        K, V, sK, sV = kx.half(), vx.half(), None, None
+    else:
+        K, sK = va.quantize(kx, bits, 1, rows, D)
+        V, sV = va.quantize(vx, bits, 1, rows, D)
+    del kx, vx
+    q = torch.randn(Hq * Lq * D, device=dev, generator=g).half()
+    out = torch.empty_like(q)
+    return va.DeviceBufs(K, V, sK, sV, q, out)
+
+
+def prefill_flops(Hq, L, Lq):
+    """Algorithmic FLOPs of a causal prefill: 2 D multiply-adds (QK and PV) per
+    visible (token, row) pair, token i seeing L - Lq + 1 + i rows."""
+    pairs = Lq * (L - Lq) + Lq * (Lq + 1) // 2
+    return 4.0 * D * Hq * pairs
+
+
+def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=10):
+    """Prompt prefill on the tcgen05 kernel: Lq tokens over a cache of L rows
+    (L = Lq: a fresh prompt), 32 query / 8 KV heads. TFLOP/s of the causal
+    work (no flops counted for masked pairs), against the measured bf16 dense
+    peak (the kernel computes fp16 x fp16 -> fp32)."""
+    b = make_prefill(va, torch, dev, fmt, Hq, Hkv, L, Lq, 5150)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    flops = prefill_flops(Hq, L, Lq)
+    peaks, kind = measured_peaks()
+    tf = flops / (ms * 1e9)
+    err = va.device_error()
+    return {"workload": f"prefill Hq={Hq} Hkv={Hkv} D={D} L={L} Lq={Lq} causal {fmt}", "ms": ms,
+            "tok_s": Lq * 1e3 / ms, "tflops": tf, "flops": flops,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "peak_kind": f"{kind} (cuBLAS bf16 burst)"},
+            "reps": reps, "device_error": err}
+
+
 def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
     """BASELINE config 3 across GPUs: one sequence of L positions split into
     contiguous ranges per rank; each rank decodes its range into per-head
@@ -621,6 +680,9 @@ def run_ours(args, rank, world):
             torch.cuda.empty_cache()
             extra["gqa_config5_paged"] = paged_leg(va, torch, dev, K)
             torch.cuda.empty_cache()
+            for pf in ("q4+", "f16+"):
+                extra[f"prefill_{pf}"] = prefill_leg(va, torch, dev, pf)
+                torch.cuda.empty_cache()
         else:
             extra["splitl_config3"] = splitl_leg(va, torch, dev, dist, world, K)
             torch.cuda.empty_cache()
@@ -666,6 +728,15 @@ def run_profile(args):
     import voltattn_b200 as va
     dev = torch.device("cuda", 0)
     fmt, L = args.fmt, args.L
+    if args.prefill_lq > 0:
+        Hq, Hkv, Lq = 32, 8, args.prefill_lq
+        b = make_prefill(va, torch, dev, fmt, Hq, Hkv, max(L, Lq), Lq, 5150)
+        for _ in range(args.warmup + args.steps):
+            va.prefill(fmt, b, Hq, Hkv, max(L, Lq), Lq, D)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": fmt, "prefill_lq": Lq, "L": max(L, Lq),
+                          "launches": args.warmup + args.steps, "device_error": va.device_error()}))
+        return
     if args.gqa_batch > 0:
         B, Hq, Hkv, Lmax, S = args.gqa_batch, 32, 8, 32768, 4
         b, lens_d, nbytes = make_gqa(va, torch, dev, 4242, fmt, B, Hq, Hkv, Lmax, S)

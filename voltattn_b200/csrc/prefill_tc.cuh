@@ -55,8 +55,9 @@ struct PrefillCfg {
     static constexpr int kThreads = 256;
     static constexpr int kRb = kD * KindTraits<K>::kBits / 8;  // code bytes per cache row
     static constexpr int kTile = kBq * kD * 2;                 // one fp16 128 x 128 tile
-    static constexpr int kSmemBytes = 1024 + 4 * kTile + 64;   // Q, K, V, P + barriers
-    static constexpr int kTmemCols = 256;                      // S and O, 128 fp32 columns each
+    // Q, K (P reuses it once S is done), V + barriers: 97 KB, 2 CTAs per SM
+    static constexpr int kSmemBytes = 1024 + 3 * kTile + 64;
+    static constexpr int kTmemCols = 256;  // S and O, 128 fp32 columns each (2 CTAs: all 512)
     static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
 };
 
@@ -144,6 +145,16 @@ __host__ __device__ constexpr uint32_t pf_off(int row, int chunk) {
     return (uint32_t)((chunk >> 3) * 16384 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
+// fp16 pair {1024 + a, 1024 + b} from two bytes a, b < 256 placed by a byte
+// permute next to the exponent byte 0x64 (1024 = 0x6400), then the code
+// offset subtracted exactly (HSUB2) and the scale applied with one rounding
+// (HMUL2): the same value as rounding code * scale from fp32.
+__device__ __forceinline__ uint32_t pf_h2(uint32_t bytes, uint32_t sel, __half2 off, __half2 sc) {
+    const uint32_t u = __byte_perm(bytes, 0x64646464u, sel);
+    const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&u), off), sc);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // Dims 8 c .. 8 c + 7 of cache row `row` (global), dequantized to fp16.
 template <Kind K>
 __device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half* scales, long long row, int c) {
@@ -152,33 +163,40 @@ __device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half*
     if constexpr (K == Kind::F16) {
         return __ldg(reinterpret_cast<const uint4*>(src) + c);
     } else {
-        const float s = __half2float(__ldg(scales + (size_t)row * 2 + (c >> 3)));
-        float v[8];
+        const __half2 sc = __half2half2(__ldg(scales + (size_t)row * 2 + (c >> 3)));
+        uint4 r;
         if constexpr (K == Kind::Q8) {
+            // signed byte + 128 = unsigned byte: 1024 + v + 128
+            const __half2 off = __float2half2_rn(1152.f);
             const uint2 w = __ldg(reinterpret_cast<const uint2*>(src) + c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                v[i] = (float)(int8_t)(w.x >> (8 * i));
-                v[4 + i] = (float)(int8_t)(w.y >> (8 * i));
-            }
+            const uint32_t a = w.x ^ 0x80808080u, b = w.y ^ 0x80808080u;
+            r.x = pf_h2(a, 0x4140, off, sc);
+            r.y = pf_h2(a, 0x4342, off, sc);
+            r.z = pf_h2(b, 0x4140, off, sc);
+            r.w = pf_h2(b, 0x4342, off, sc);
         } else if constexpr (K == Kind::Q4) {
             // byte b of the chunk holds dims 2b (low nibble) and 2b+1; nibble = code + 8
+            const __half2 off = __float2half2_rn(1032.f);
             const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src) + c);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = (float)((int)((w >> (4 * i)) & 0xFu) - 8);
+            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+            const uint32_t p01 = __byte_perm(lo, hi, 0x5140), p23 = __byte_perm(lo, hi, 0x7362);
+            r.x = pf_h2(p01, 0x4140, off, sc);
+            r.y = pf_h2(p01, 0x4342, off, sc);
+            r.z = pf_h2(p23, 0x4140, off, sc);
+            r.w = pf_h2(p23, 0x4342, off, sc);
         } else {
             // dims 8c .. 8c+7: bits 24c .. 24c+23 of the row, field = code + 4
+            const __half2 off = __float2half2_rn(1028.f);
             const uint32_t x = (uint32_t)__ldg(src + 3 * c) | ((uint32_t)__ldg(src + 3 * c + 1) << 8) |
                                ((uint32_t)__ldg(src + 3 * c + 2) << 16);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = (float)((int)((x >> (3 * i)) & 7u) - 4);
-        }
-        uint4 r;
-        uint32_t* rw = reinterpret_cast<uint32_t*>(&r);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const __half2 h = __floats2half2_rn(v[2 * i] * s, v[2 * i + 1] * s);
-            rw[i] = *reinterpret_cast<const uint32_t*>(&h);
+            // fields to bytes: f0 f1 f2 f3 -> lo, f4..f7 -> hi
+            const uint32_t lo = (x & 7u) | ((x << 5) & 0x700u) | ((x << 10) & 0x70000u) | ((x << 15) & 0x7000000u);
+            const uint32_t y = x >> 12;
+            const uint32_t hi = (y & 7u) | ((y << 5) & 0x700u) | ((y << 10) & 0x70000u) | ((y << 15) & 0x7000000u);
+            r.x = pf_h2(lo, 0x4140, off, sc);
+            r.y = pf_h2(lo, 0x4342, off, sc);
+            r.z = pf_h2(hi, 0x4140, off, sc);
+            r.w = pf_h2(hi, 0x4342, off, sc);
         }
         return r;
     }
@@ -189,13 +207,13 @@ __device__ __forceinline__ void sts128_generic(uint8_t* base, uint32_t off, uint
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::kThreads, 1) prefill_tc_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const PrefillParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* sQ = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sK = sQ + C::kTile;
     uint8_t* sV = sK + C::kTile;
-    uint8_t* sP = sV + C::kTile;
-    uint64_t* bar_s = reinterpret_cast<uint64_t*>(sP + C::kTile);
+    uint8_t* sP = sK;  // P overwrites K once S = Q K^T is complete
+    uint64_t* bar_s = reinterpret_cast<uint64_t*>(sV + C::kTile);
     uint64_t* bar_o = bar_s + 1;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
     volatile int* fail = reinterpret_cast<volatile int*>(tslot + 1);
@@ -281,31 +299,42 @@ __global__ void __launch_bounds__(C::kThreads, 1) prefill_tc_kernel(const Prefil
         }
         // 3. online softmax of this thread's token row; P -> sP; rescale O
         if (softmax_warp) {
-            float s[C::kBk];
-#pragma unroll
-            for (int cb = 0; cb < C::kBk / 32; ++cb) tmem_ld32(tS + lane_addr + 32 * cb, s + 32 * cb);
+            // two passes over S in TMEM (the row maximum, then the weights):
+            // 32 columns in registers at a time
             float bm = kNegMax;
 #pragma unroll
-            for (int j = 0; j < C::kBk; ++j) {
-                const bool ok = r0 + j <= vis && r0 + j < p.L;
-                s[j] = ok ? s[j] * qk_scale : -INFINITY;
-                bm = fmaxf(bm, s[j]);
+            for (int cb = 0; cb < C::kBk / 32; ++cb) {
+                float s[32];
+                tmem_ld32(tS + lane_addr + 32 * cb, s);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const long long gr = r0 + 32 * cb + j;
+                    if (gr <= vis && gr < p.L) bm = fmaxf(bm, s[j] * qk_scale);
+                }
             }
             const float mnew = fmaxf(m, bm);
             const float corr = fast_exp2(m - mnew);
             m = mnew;
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                uint32_t w[4];
+            for (int cb = 0; cb < C::kBk / 32; ++cb) {
+                float s[32];
+                tmem_ld32(tS + lane_addr + 32 * cb, s);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float a = fast_exp2(s[8 * c + 2 * i] - mnew), b = fast_exp2(s[8 * c + 2 * i + 1] - mnew);
-                    sum += a + b;
-                    const __half2 hp = __floats2half2_rn(a, b);
-                    w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 8 * c4 + 2 * i;
+                        const long long gr = r0 + 32 * cb + j;
+                        const float a = (gr <= vis && gr < p.L) ? fast_exp2(s[j] * qk_scale - mnew) : 0.f;
+                        const float b = (gr + 1 <= vis && gr + 1 < p.L) ? fast_exp2(s[j + 1] * qk_scale - mnew) : 0.f;
+                        sum += a + b;
+                        const __half2 hp = __floats2half2_rn(a, b);
+                        w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                    }
+                    sts128_generic(sP, pf_off(row, 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
                 }
-                sts128_generic(sP, pf_off(row, c), make_uint4(w[0], w[1], w[2], w[3]));
             }
             l = l * corr + sum;
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
