@@ -13,15 +13,16 @@
 // KV head h / (Hq / Hkv)). Token i (0-based) sees cache rows
 // [0, L - Lq + i] (causal). q, out: fp16 [Hq][Lq][D]; cache [Hkv][L] rows.
 //
-// One CTA per (query head, block of 128 tokens), 8 warps, 1 CTA per SM.
-// Per block of 128 cache rows:
+// One CTA per (query head, block of 128 tokens), 8 warps, 2 CTAs per SM (the
+// two CTAs' phases interleave). Per block of 128 cache rows:
 //   1. all warps dequantize the block's K and V rows to fp16 into shared
-//      memory (plain loads; code * scale rounded to fp16);
+//      memory (all loads of a thread first, then code * scale, one rounding);
 //   2. one thread issues S = Q K^T as 8 tcgen05.mma (M = 128 tokens,
 //      N = 128 rows, K = 16 dims each) into TMEM columns [0, 128);
-//   3. warps 0..3 (TMEM lanes 0..127, one token row per thread) read S,
-//      mask, run the online softmax in registers, write P (fp16) to shared
-//      memory and rescale the running O in TMEM when the row maximum moved;
+//   3. warps 0..3 (TMEM lanes 0..127, one token row per thread) read S twice
+//      (row maximum, then weights), mask only blocks on the diagonal, write
+//      P (fp16) over the K tile, which S no longer needs, and rescale the
+//      running O in TMEM when the row maximum moved;
 //   4. one thread issues O += P V as 8 tcgen05.mma (N = 128 dims, K = 16
 //      rows each) into TMEM columns [128, 256).
 // The tiles use the canonical 128-byte-swizzled layout: two 64-element
@@ -125,6 +126,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// The same load without the wait: two or more go out back to back, then one
+// tmem_wait_ld_only, after which tmem_tie32 ties each group of 32 registers to
+// the wait (an empty asm that redefines them), so no use is scheduled earlier.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld_only() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_tie32(uint32_t* r) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
     uint32_t r[32];
 #pragma unroll
@@ -155,21 +180,57 @@ __device__ __forceinline__ uint32_t pf_h2(uint32_t bytes, uint32_t sel, __half2 
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Dims 8 c .. 8 c + 7 of cache row `row` (global), dequantized to fp16.
+// Raw codes of dims 8 c .. 8 c + 7 of one cache row and the row's group
+// scale. A thread loads all of its chunks first and converts them after, so
+// the global-load latencies overlap instead of following one another (the
+// shared-memory stores in between are through generic pointers, which the
+// compiler will not move loads across).
 template <Kind K>
-__device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half* scales, long long row, int c) {
+struct PfRaw {
+    uint32_t w[K == Kind::F16 ? 4 : K == Kind::Q8 ? 2 : 1];
+    __half sc;
+};
+
+template <Kind K>
+__device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* scales, long long row, int c) {
     constexpr int kRb = PrefillCfg<K>::kRb;
     const uint8_t* src = codes + (size_t)row * kRb;
+    PfRaw<K> r;
     if constexpr (K == Kind::F16) {
-        return __ldg(reinterpret_cast<const uint4*>(src) + c);
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + c);
+        r.w[0] = v.x;
+        r.w[1] = v.y;
+        r.w[2] = v.z;
+        r.w[3] = v.w;
+        r.sc = __float2half(0.f);
     } else {
-        const __half2 sc = __half2half2(__ldg(scales + (size_t)row * 2 + (c >> 3)));
+        r.sc = __ldg(scales + (size_t)row * 2 + (c >> 3));
+        if constexpr (K == Kind::Q8) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + c);
+            r.w[0] = v.x;
+            r.w[1] = v.y;
+        } else if constexpr (K == Kind::Q4) {
+            r.w[0] = __ldg(reinterpret_cast<const uint32_t*>(src) + c);
+        } else {  // bits 24c .. 24c+23 of the row
+            r.w[0] = (uint32_t)__ldg(src + 3 * c) | ((uint32_t)__ldg(src + 3 * c + 1) << 8) |
+                     ((uint32_t)__ldg(src + 3 * c + 2) << 16);
+        }
+    }
+    return r;
+}
+
+// The chunk as 8 fp16 values.
+template <Kind K>
+__device__ __forceinline__ uint4 pf_convert(const PfRaw<K>& raw) {
+    if constexpr (K == Kind::F16) {
+        return make_uint4(raw.w[0], raw.w[1], raw.w[2], raw.w[3]);
+    } else {
+        const __half2 sc = __half2half2(raw.sc);
         uint4 r;
         if constexpr (K == Kind::Q8) {
             // signed byte + 128 = unsigned byte: 1024 + v + 128
             const __half2 off = __float2half2_rn(1152.f);
-            const uint2 w = __ldg(reinterpret_cast<const uint2*>(src) + c);
-            const uint32_t a = w.x ^ 0x80808080u, b = w.y ^ 0x80808080u;
+            const uint32_t a = raw.w[0] ^ 0x80808080u, b = raw.w[1] ^ 0x80808080u;
             r.x = pf_h2(a, 0x4140, off, sc);
             r.y = pf_h2(a, 0x4342, off, sc);
             r.z = pf_h2(b, 0x4140, off, sc);
@@ -177,7 +238,7 @@ __device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half*
         } else if constexpr (K == Kind::Q4) {
             // byte b of the chunk holds dims 2b (low nibble) and 2b+1; nibble = code + 8
             const __half2 off = __float2half2_rn(1032.f);
-            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src) + c);
+            const uint32_t w = raw.w[0];
             const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
             const uint32_t p01 = __byte_perm(lo, hi, 0x5140), p23 = __byte_perm(lo, hi, 0x7362);
             r.x = pf_h2(p01, 0x4140, off, sc);
@@ -185,11 +246,9 @@ __device__ __forceinline__ uint4 pf_dequant8(const uint8_t* codes, const __half*
             r.z = pf_h2(p23, 0x4140, off, sc);
             r.w = pf_h2(p23, 0x4342, off, sc);
         } else {
-            // dims 8c .. 8c+7: bits 24c .. 24c+23 of the row, field = code + 4
+            // field = code + 4; fields f0..f3 -> bytes of lo, f4..f7 -> bytes of hi
             const __half2 off = __float2half2_rn(1028.f);
-            const uint32_t x = (uint32_t)__ldg(src + 3 * c) | ((uint32_t)__ldg(src + 3 * c + 1) << 8) |
-                               ((uint32_t)__ldg(src + 3 * c + 2) << 16);
-            // fields to bytes: f0 f1 f2 f3 -> lo, f4..f7 -> hi
+            const uint32_t x = raw.w[0];
             const uint32_t lo = (x & 7u) | ((x << 5) & 0x700u) | ((x << 10) & 0x70000u) | ((x << 15) & 0x7000000u);
             const uint32_t y = x >> 12;
             const uint32_t hi = (y & 7u) | ((y << 5) & 0x700u) | ((y << 10) & 0x70000u) | ((y << 15) & 0x7000000u);
@@ -263,18 +322,24 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
 
     for (int kb = 0; kb < nkb; ++kb) {
         const long long r0 = (long long)kb * C::kBk;
-        // 1. dequantize the block's K and V rows (rows past L: zero, masked)
-        for (int i = tid; i < C::kBk * 16; i += C::kThreads) {
-            const int r = i >> 4, c = i & 15;
-            const long long gr = r0 + r;
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-            if (gr < p.L) {
-                const long long grow = (long long)hk * p.L + gr;
-                kv = pf_dequant8<C::kKind>(p.K, p.scK, grow, c);
-                vv = pf_dequant8<C::kKind>(p.V, p.scV, grow, c);
+        // 1. dequantize the block's K and V rows (rows past L repeat row L - 1:
+        //    masked, weight 0)
+        {
+            constexpr int kPer = C::kBk * 16 / C::kThreads;  // chunks per thread
+            PfRaw<C::kKind> rk[kPer], rv[kPer];
+#pragma unroll
+            for (int t = 0; t < kPer; ++t) {
+                const int i = tid + t * C::kThreads;
+                const long long grow = (long long)hk * p.L + min(r0 + (i >> 4), (long long)p.L - 1);
+                rk[t] = pf_load<C::kKind>(p.K, p.scK, grow, i & 15);
+                rv[t] = pf_load<C::kKind>(p.V, p.scV, grow, i & 15);
             }
-            sts128_generic(sK, pf_off(r, c), kv);
-            sts128_generic(sV, pf_off(r, c), vv);
+#pragma unroll
+            for (int t = 0; t < kPer; ++t) {
+                const int i = tid + t * C::kThreads;
+                sts128_generic(sK, pf_off(i >> 4, i & 15), pf_convert<C::kKind>(rk[t]));
+                sts128_generic(sV, pf_off(i >> 4, i & 15), pf_convert<C::kKind>(rv[t]));
+            }
         }
         fence_proxy_async_smem();
         tc05_fence_before();
@@ -299,23 +364,36 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         }
         // 3. online softmax of this thread's token row; P -> sP; rescale O
         if (softmax_warp) {
-            // two passes over S in TMEM (the row maximum, then the weights):
-            // 32 columns in registers at a time
-            float bm = kNegMax;
+            // two passes over S in TMEM (the row maximum, then the weights).
+            // Columns j <= lim of this block are visible to the row: all of
+            // them below the diagonal, none past the cache's end.
+            const int lim = (int)max(-1ll, min(min(vis, (long long)p.L - 1) - r0, (long long)C::kBk - 1));
+            const bool full = lim == C::kBk - 1;
+            float bm0 = kNegMax, bm1 = kNegMax;
 #pragma unroll
-            for (int cb = 0; cb < C::kBk / 32; ++cb) {
-                float s[32];
-                tmem_ld32(tS + lane_addr + 32 * cb, s);
+            for (int cp = 0; cp < C::kBk / 64; ++cp) {
+                uint32_t s[2][32];
+                tmem_ld32_nowait(tS + lane_addr + 64 * cp, s[0]);
+                tmem_ld32_nowait(tS + lane_addr + 64 * cp + 32, s[1]);
+                tmem_wait_ld_only();
+                tmem_tie32(s[0]);
+                tmem_tie32(s[1]);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const long long gr = r0 + 32 * cb + j;
-                    if (gr <= vis && gr < p.L) bm = fmaxf(bm, s[j] * qk_scale);
+                for (int j = 0; j < 64; j += 2) {
+                    const float x0 = __uint_as_float(s[j >> 5][j & 31]), x1 = __uint_as_float(s[j >> 5][(j & 31) + 1]);
+                    if (full) {
+                        bm0 = fmaxf(bm0, x0);
+                        bm1 = fmaxf(bm1, x1);
+                    } else {
+                        if (64 * cp + j <= lim) bm0 = fmaxf(bm0, x0);
+                        if (64 * cp + j + 1 <= lim) bm1 = fmaxf(bm1, x1);
+                    }
                 }
             }
-            const float mnew = fmaxf(m, bm);
+            const float mnew = fmaxf(m, fmaxf(bm0, bm1) * qk_scale);
             const float corr = fast_exp2(m - mnew);
             m = mnew;
-            float sum = 0.f;
+            float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
             for (int cb = 0; cb < C::kBk / 32; ++cb) {
                 float s[32];
@@ -326,16 +404,21 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 8 * c4 + 2 * i;
-                        const long long gr = r0 + 32 * cb + j;
-                        const float a = (gr <= vis && gr < p.L) ? fast_exp2(s[j] * qk_scale - mnew) : 0.f;
-                        const float b = (gr + 1 <= vis && gr + 1 < p.L) ? fast_exp2(s[j + 1] * qk_scale - mnew) : 0.f;
-                        sum += a + b;
+                        float a = fast_exp2(fmaf(s[j], qk_scale, -mnew));
+                        float b = fast_exp2(fmaf(s[j + 1], qk_scale, -mnew));
+                        if (!full) {
+                            a = 32 * cb + j <= lim ? a : 0.f;
+                            b = 32 * cb + j + 1 <= lim ? b : 0.f;
+                        }
+                        sum0 += a;
+                        sum1 += b;
                         const __half2 hp = __floats2half2_rn(a, b);
                         w[i] = *reinterpret_cast<const uint32_t*>(&hp);
                     }
                     sts128_generic(sP, pf_off(row, 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
                 }
             }
+            const float sum = sum0 + sum1;
             l = l * corr + sum;
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
