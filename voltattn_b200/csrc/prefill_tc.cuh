@@ -57,7 +57,7 @@ struct PrefillCfg {
     static constexpr int kRb = kD * KindTraits<K>::kBits / 8;  // code bytes per cache row
     static constexpr int kTile = kBq * kD * 2;                 // one fp16 128 x 128 tile
     // Q, K (P reuses it once S is done), V + barriers: 97 KB, 2 CTAs per SM
-    static constexpr int kSmemBytes = 1024 + 3 * kTile + 64;
+    static constexpr int kSmemBytes = 1024 + 3 * kTile + 64 + 2 * kBq * 4;  // + row-max exchange
     static constexpr int kTmemCols = 256;  // S and O, 128 fp32 columns each (2 CTAs: all 512)
     static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
 };
@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     uint64_t* bar_o = bar_s + 1;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
     volatile int* fail = reinterpret_cast<volatile int*>(tslot + 1);
+    float* xch = reinterpret_cast<float*>(bar_s + 8);  // [2][128]: the half-rows' maxima / sums
 
     constexpr int D = C::kD;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -313,12 +314,14 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     // cache rows this CTA needs: [0, last], last = min(L - 1, off0 + q0 + 127)
     const long long last = min((long long)p.L - 1, off0 + q0 + C::kBq - 1);
     const int nkb = (int)(last / C::kBk) + 1;
-    const bool softmax_warp = warp < 4;
-    const int row = tid;  // token row of softmax threads (TMEM lane)
+    // softmax: every thread; warpgroup hf takes columns [64 hf, 64 hf + 64)
+    // of its token row (TMEM lane = row) of S, P and O
+    const int hf = warp >> 2;
+    const int row = tid & 127;
     const long long vis = off0 + q0 + row;  // last visible cache row of this token
     const float qk_scale = rsqrtf((float)D) * kLog2e;
     float m = kNegMax, l = 0.f;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_addr = ((uint32_t)((warp & 3) * 32) << 16) + 64 * hf;
 
     for (int kb = 0; kb < nkb; ++kb) {
         const long long r0 = (long long)kb * C::kBk;
@@ -362,19 +365,18 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             if (tid == 0) *fail = 1;
             break;
         }
-        // 3. online softmax of this thread's token row; P -> sP; rescale O
-        if (softmax_warp) {
+        // 3. online softmax of this thread's half token row; P -> sP; rescale O
+        {
             // two passes over S in TMEM (the row maximum, then the weights).
             // Columns j <= lim of this block are visible to the row: all of
             // them below the diagonal, none past the cache's end.
-            const int lim = (int)max(-1ll, min(min(vis, (long long)p.L - 1) - r0, (long long)C::kBk - 1));
-            const bool full = lim == C::kBk - 1;
+            const int lim = (int)max(-1ll, min(min(vis, (long long)p.L - 1) - r0, (long long)C::kBk - 1)) - 64 * hf;
+            const bool full = lim >= 63;
             float bm0 = kNegMax, bm1 = kNegMax;
-#pragma unroll
-            for (int cp = 0; cp < C::kBk / 64; ++cp) {
+            {
                 uint32_t s[2][32];
-                tmem_ld32_nowait(tS + lane_addr + 64 * cp, s[0]);
-                tmem_ld32_nowait(tS + lane_addr + 64 * cp + 32, s[1]);
+                tmem_ld32_nowait(tS + lane_addr, s[0]);
+                tmem_ld32_nowait(tS + lane_addr + 32, s[1]);
                 tmem_wait_ld_only();
                 tmem_tie32(s[0]);
                 tmem_tie32(s[1]);
@@ -385,17 +387,21 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                         bm0 = fmaxf(bm0, x0);
                         bm1 = fmaxf(bm1, x1);
                     } else {
-                        if (64 * cp + j <= lim) bm0 = fmaxf(bm0, x0);
-                        if (64 * cp + j + 1 <= lim) bm1 = fmaxf(bm1, x1);
+                        if (j <= lim) bm0 = fmaxf(bm0, x0);
+                        if (j + 1 <= lim) bm1 = fmaxf(bm1, x1);
                     }
                 }
             }
-            const float mnew = fmaxf(m, fmaxf(bm0, bm1) * qk_scale);
+            // the row's maximum over both halves
+            xch[hf * 128 + row] = fmaxf(bm0, bm1);
+            __syncthreads();
+            const float bm = fmaxf(xch[row], xch[128 + row]);
+            const float mnew = fmaxf(m, bm * qk_scale);
             const float corr = fast_exp2(m - mnew);
             m = mnew;
             float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-            for (int cb = 0; cb < C::kBk / 32; ++cb) {
+            for (int cb = 0; cb < 2; ++cb) {
                 float s[32];
                 tmem_ld32(tS + lane_addr + 32 * cb, s);
 #pragma unroll
@@ -403,26 +409,25 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                     uint32_t w[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const int j = 8 * c4 + 2 * i;
-                        float a = fast_exp2(fmaf(s[j], qk_scale, -mnew));
-                        float b = fast_exp2(fmaf(s[j + 1], qk_scale, -mnew));
+                        const int j = 32 * cb + 8 * c4 + 2 * i;  // column 64 hf + j
+                        float a = fast_exp2(fmaf(s[j & 31], qk_scale, -mnew));
+                        float b = fast_exp2(fmaf(s[(j & 31) + 1], qk_scale, -mnew));
                         if (!full) {
-                            a = 32 * cb + j <= lim ? a : 0.f;
-                            b = 32 * cb + j + 1 <= lim ? b : 0.f;
+                            a = j <= lim ? a : 0.f;
+                            b = j + 1 <= lim ? b : 0.f;
                         }
                         sum0 += a;
                         sum1 += b;
                         const __half2 hp = __floats2half2_rn(a, b);
                         w[i] = *reinterpret_cast<const uint32_t*>(&hp);
                     }
-                    sts128_generic(sP, pf_off(row, 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
+                    sts128_generic(sP, pf_off(row, 8 * hf + 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
                 }
             }
-            const float sum = sum0 + sum1;
-            l = l * corr + sum;
+            l = l * corr + (sum0 + sum1);  // this half's share of the row sum
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-                for (int cb = 0; cb < D / 32; ++cb) {
+                for (int cb = 0; cb < 2; ++cb) {
                     float o[32];
                     tmem_ld32(tO + lane_addr + 32 * cb, o);
 #pragma unroll
@@ -455,16 +460,19 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             break;
         }
     }
-    // epilogue: out = O / l for the CTA's valid tokens
+    // epilogue: out = O / l for the CTA's valid tokens (l: both halves' sums)
     __syncthreads();
-    if (softmax_warp && !*fail) {
-        const float inv = 1.f / l;
+    xch[hf * 128 + row] = l;
+    __syncthreads();
+    if (!*fail) {
+        const float inv = 1.f / (xch[row] + xch[128 + row]);
 #pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
+        for (int cb = 0; cb < 2; ++cb) {
             float o[32];
             tmem_ld32(tO + lane_addr + 32 * cb, o);
             if (q0 + row < p.Lq) {
-                uint4* dst = reinterpret_cast<uint4*>(p.out + ((size_t)h * p.Lq + q0 + row) * D + 32 * cb);
+                uint4* dst =
+                    reinterpret_cast<uint4*>(p.out + ((size_t)h * p.Lq + q0 + row) * D + 64 * hf + 32 * cb);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t w[4];
