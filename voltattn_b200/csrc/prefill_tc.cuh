@@ -19,10 +19,12 @@
 //      memory (all loads of a thread first, then code * scale, one rounding);
 //   2. one thread issues S = Q K^T as 8 tcgen05.mma (M = 128 tokens,
 //      N = 128 rows, K = 16 dims each) into TMEM columns [0, 128);
-//   3. warps 0..3 (TMEM lanes 0..127, one token row per thread) read S twice
-//      (row maximum, then weights), mask only blocks on the diagonal, write
-//      P (fp16) over the K tile, which S no longer needs, and rescale the
-//      running O in TMEM when the row maximum moved;
+//   3. all 8 warps run the softmax: thread (warpgroup hf, TMEM lane r) takes
+//      columns [64 hf, 64 hf + 64) of token row r. It reads S twice (row
+//      maximum, exchanged with the other half through shared memory, then
+//      the weights), masks only blocks on the diagonal, writes its half of P
+//      (fp16) over the K tile, which S no longer needs, and rescales its half
+//      of the running O in TMEM when the row maximum moved;
 //   4. one thread issues O += P V as 8 tcgen05.mma (N = 128 dims, K = 16
 //      rows each) into TMEM columns [128, 256).
 // The tiles use the canonical 128-byte-swizzled layout: two 64-element
