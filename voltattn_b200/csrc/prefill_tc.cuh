@@ -62,6 +62,7 @@ struct PrefillCfg {
     static constexpr int kSmemBytes = 1024 + 3 * kTile + 64 + 2 * kBq * 4;  // + row-max exchange
     static constexpr int kTmemCols = 256;  // S and O, 128 fp32 columns each (2 CTAs: all 512)
     static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
+    static_assert((kThreads / 16) % 8 == 0, "dequant rows of a thread share the swizzle phase");
 };
 
 // ---- tcgen05 / TMEM wrappers (PTX ISA 8.6+, sm_100a) ---------------------------------------
@@ -330,20 +331,33 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         // 1. dequantize the block's K and V rows (rows past L repeat row L - 1:
         //    masked, weight 0)
         {
+            // thread tid takes chunk c = tid % 16 of rows tid / 16 + 16 t: one
+            // base row per block, the rest constant offsets (rows 16 apart keep
+            // the swizzle phase, so the shared-memory offsets are constant too)
             constexpr int kPer = C::kBk * 16 / C::kThreads;  // chunks per thread
+            constexpr int kRowStep = C::kThreads / 16;
+            const int c = tid & 15, rr = tid >> 4;
             PfRaw<C::kKind> rk[kPer], rv[kPer];
+            if (r0 + C::kBk <= p.L) {
+                const long long grow = (long long)hk * p.L + r0 + rr;
 #pragma unroll
-            for (int t = 0; t < kPer; ++t) {
-                const int i = tid + t * C::kThreads;
-                const long long grow = (long long)hk * p.L + min(r0 + (i >> 4), (long long)p.L - 1);
-                rk[t] = pf_load<C::kKind>(p.K, p.scK, grow, i & 15);
-                rv[t] = pf_load<C::kKind>(p.V, p.scV, grow, i & 15);
+                for (int t = 0; t < kPer; ++t) {
+                    rk[t] = pf_load<C::kKind>(p.K, p.scK, grow + kRowStep * t, c);
+                    rv[t] = pf_load<C::kKind>(p.V, p.scV, grow + kRowStep * t, c);
+                }
+            } else {  // the cache's last block: rows past L repeat row L - 1 (masked, weight 0)
+#pragma unroll
+                for (int t = 0; t < kPer; ++t) {
+                    const long long grow = (long long)hk * p.L + min(r0 + rr + kRowStep * t, (long long)p.L - 1);
+                    rk[t] = pf_load<C::kKind>(p.K, p.scK, grow, c);
+                    rv[t] = pf_load<C::kKind>(p.V, p.scV, grow, c);
+                }
             }
+            const uint32_t so = pf_off(rr, c);
 #pragma unroll
             for (int t = 0; t < kPer; ++t) {
-                const int i = tid + t * C::kThreads;
-                sts128_generic(sK, pf_off(i >> 4, i & 15), pf_convert<C::kKind>(rk[t]));
-                sts128_generic(sV, pf_off(i >> 4, i & 15), pf_convert<C::kKind>(rv[t]));
+                sts128_generic(sK, so + kRowStep * 128 * t, pf_convert<C::kKind>(rk[t]));
+                sts128_generic(sV, so + kRowStep * 128 * t, pf_convert<C::kKind>(rv[t]));
             }
         }
         fence_proxy_async_smem();
