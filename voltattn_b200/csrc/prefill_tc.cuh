@@ -168,6 +168,33 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// sm_100 float forms that halve the softmax's instruction count: a
+// three-input maximum, and paired fp32 FMA / add (two lanes in one 64-bit
+// register pair).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // Byte offset of (row, 16-byte chunk 0..15) in a swizzled 128 x 128 fp16 tile.
 __host__ __device__ constexpr uint32_t pf_off(int row, int chunk) {
     return (uint32_t)((chunk >> 3) * 16384 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
@@ -400,8 +427,8 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                 for (int j = 0; j < 64; j += 2) {
                     const float x0 = __uint_as_float(s[j >> 5][j & 31]), x1 = __uint_as_float(s[j >> 5][(j & 31) + 1]);
                     if (full) {
-                        bm0 = fmaxf(bm0, x0);
-                        bm1 = fmaxf(bm1, x1);
+                        if (j & 2) bm1 = fmax3f(bm1, x0, x1);
+                        else bm0 = fmax3f(bm0, x0, x1);
                     } else {
                         if (j <= lim) bm0 = fmaxf(bm0, x0);
                         if (j + 1 <= lim) bm1 = fmaxf(bm1, x1);
@@ -415,7 +442,8 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             const float mnew = fmaxf(m, bm * qk_scale);
             const float corr = fast_exp2(m - mnew);
             m = mnew;
-            float sum0 = 0.f, sum1 = 0.f;
+            float2 sum2 = make_float2(0.f, 0.f);
+            const float2 sc2 = make_float2(qk_scale, qk_scale), nm2 = make_float2(-mnew, -mnew);
 #pragma unroll
             for (int cb = 0; cb < 2; ++cb) {
                 float s[32];
@@ -426,21 +454,21 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 32 * cb + 8 * c4 + 2 * i;  // column 64 hf + j
-                        float a = fast_exp2(fmaf(s[j & 31], qk_scale, -mnew));
-                        float b = fast_exp2(fmaf(s[(j & 31) + 1], qk_scale, -mnew));
+                        const float2 x = ffma2(make_float2(s[j & 31], s[(j & 31) + 1]), sc2, nm2);
+                        float a = fast_exp2(x.x);
+                        float b = fast_exp2(x.y);
                         if (!full) {
                             a = j <= lim ? a : 0.f;
                             b = j + 1 <= lim ? b : 0.f;
                         }
-                        sum0 += a;
-                        sum1 += b;
+                        sum2 = fadd2(sum2, make_float2(a, b));
                         const __half2 hp = __floats2half2_rn(a, b);
                         w[i] = *reinterpret_cast<const uint32_t*>(&hp);
                     }
                     sts128_generic(sP, pf_off(row, 8 * hf + 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
                 }
             }
-            l = l * corr + (sum0 + sum1);  // this half's share of the row sum
+            l = l * corr + (sum2.x + sum2.y);  // this half's share of the row sum
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
                 for (int cb = 0; cb < 2; ++cb) {
