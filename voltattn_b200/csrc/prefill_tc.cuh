@@ -23,10 +23,10 @@
 //      columns [64 hf, 64 hf + 64) of token row r. It reads S twice (row
 //      maximum, exchanged with the other half through shared memory, then
 //      the weights), masks only blocks on the diagonal, writes its half of P
-//      (fp16) over the K tile, which S no longer needs, and rescales its half
-//      of the running O in TMEM when the row maximum moved;
-//   4. one thread issues O += P V as 8 tcgen05.mma (N = 128 dims, K = 16
-//      rows each) into TMEM columns [128, 256).
+//      (fp16 pairs) into S columns it has read, and rescales its half of the
+//      running O in TMEM when the row maximum moved;
+//   4. one thread issues O += P V as 8 tcgen05.mma with A = P read from TMEM
+//      (N = 128 dims, K = 16 rows each) into TMEM columns [128, 256).
 // The tiles use the canonical 128-byte-swizzled layout: two 64-element
 // panels of 128 rows, row r of a panel at r * 128 bytes, 16-byte chunk c at
 // (c ^ (r & 7)) * 16. The K tile is read K-major (rows = N), the V tile,
@@ -58,7 +58,7 @@ struct PrefillCfg {
     static constexpr int kThreads = 256;
     static constexpr int kRb = kD * KindTraits<K>::kBits / 8;  // code bytes per cache row
     static constexpr int kTile = kBq * kD * 2;                 // one fp16 128 x 128 tile
-    // Q, K (P reuses it once S is done), V + barriers: 97 KB, 2 CTAs per SM
+    // Q, K, V + barriers and the row-max exchange: 100 KB, 2 CTAs per SM
     static constexpr int kSmemBytes = 1024 + 3 * kTile + 64 + 2 * kBq * 4;  // + row-max exchange
     static constexpr int kTmemCols = 256;  // S and O, 128 fp32 columns each (2 CTAs: all 512)
     static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
@@ -103,6 +103,27 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+// The same with A (M x K, fp16) read from TMEM: lane m holds row m, 32-bit
+// column c holds elements 2c (low half) and 2c + 1.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
 // Arrives on the mbarrier once all tcgen05.mma issued so far by this thread complete.
@@ -301,7 +322,6 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     uint8_t* sQ = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sK = sQ + C::kTile;
     uint8_t* sV = sK + C::kTile;
-    uint8_t* sP = sK;  // P overwrites K once S = Q K^T is complete
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(sV + C::kTile);
     uint64_t* bar_o = bar_s + 1;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
@@ -337,7 +357,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     tc05_fence_after();
     const uint32_t tbase = *tslot;
     const uint32_t tS = tbase, tO = tbase + 128;
-    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV), sPa = smem_u32(sP);
+    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
     constexpr uint32_t kIdescS = umma_idesc_f16(128, 128, false);
     constexpr uint32_t kIdescO = umma_idesc_f16(128, 128, true);
 
@@ -443,6 +463,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             const float corr = fast_exp2(m - mnew);
             m = mnew;
             float2 sum2 = make_float2(0.f, 0.f);
+            uint32_t pw[32];  // P of keys 64 hf .. 64 hf + 63 as fp16 pairs
             const float2 sc2 = make_float2(qk_scale, qk_scale), nm2 = make_float2(-mnew, -mnew);
 #pragma unroll
             for (int cb = 0; cb < 2; ++cb) {
@@ -450,7 +471,6 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                 tmem_ld32(tS + lane_addr + 32 * cb, s);
 #pragma unroll
                 for (int c4 = 0; c4 < 4; ++c4) {
-                    uint32_t w[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 32 * cb + 8 * c4 + 2 * i;  // column 64 hf + j
@@ -463,11 +483,14 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                         }
                         sum2 = fadd2(sum2, make_float2(a, b));
                         const __half2 hp = __floats2half2_rn(a, b);
-                        w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                        pw[j >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
                     }
-                    sts128_generic(sP, pf_off(row, 8 * hf + 4 * cb + c4), make_uint4(w[0], w[1], w[2], w[3]));
                 }
             }
+            // P into the first 32 of this half's S columns (all read above), the
+            // A operand of O += P V
+            tmem_st32_u(tS + lane_addr, pw);
+            tmem_wait_st();
             l = l * corr + (sum2.x + sum2.y);  // this half's share of the row sum
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
@@ -481,7 +504,6 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
                 tmem_wait_st();
             }
         }
-        fence_proxy_async_smem();
         tc05_fence_before();
         __syncthreads();
         // 4. O += P V
@@ -489,10 +511,10 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             tc05_fence_after();
 #pragma unroll
             for (int kk = 0; kk < C::kBk / 16; ++kk) {
-                const uint32_t oa = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                // keys 16 kk .. 16 kk + 15: TMEM columns 64 (kk / 4) + 8 (kk % 4)
+                const uint32_t ta = tS + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
                 const uint32_t ob = (uint32_t)(kk * 16 * 128);  // 16 cache rows of 128 bytes per panel
-                umma_f16(tO, umma_desc_sw128(sPa + oa, 16, 1024), umma_desc_sw128(sVa + ob, 16384, 1024), kIdescO,
-                         kb > 0 || kk > 0);
+                umma_f16_ts(tO, ta, umma_desc_sw128(sVa + ob, 16384, 1024), kIdescO, kb > 0 || kk > 0);
             }
             umma_commit(bar_o);
         }
