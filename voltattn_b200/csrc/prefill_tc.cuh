@@ -16,7 +16,8 @@
 // One CTA per (query head, block of 128 tokens), 8 warps, 2 CTAs per SM (the
 // two CTAs' phases interleave). Per block of 128 cache rows:
 //   1. all warps dequantize the block's K and V rows to fp16 into shared
-//      memory (all loads of a thread first, then code * scale, one rounding);
+//      memory (all loads of a thread first, then code * scale, one rounding):
+//      K while the previous block's PV runs, V while this block's S runs;
 //   2. one thread issues S = Q K^T as 8 tcgen05.mma (M = 128 tokens,
 //      N = 128 rows, K = 16 dims each) into TMEM columns [0, 128);
 //   3. all 8 warps run the softmax: thread (warpgroup hf, TMEM lane r) takes
@@ -373,44 +374,32 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     float m = kNegMax, l = 0.f;
     const uint32_t lane_addr = ((uint32_t)((warp & 3) * 32) << 16) + 64 * hf;
 
-    for (int kb = 0; kb < nkb; ++kb) {
+    // one matrix (K or V) of cache block kb, dequantized into its tile. Thread
+    // tid takes chunk c = tid % 16 of rows tid / 16 + 16 t: one base row per
+    // block, the rest constant offsets (rows 16 apart keep the swizzle phase,
+    // so the shared-memory offsets are constant too). All loads go out first.
+    const auto dequant = [&](int kb, const uint8_t* codes, const __half* scales, uint8_t* dst) {
+        constexpr int kPer = C::kBk * 16 / C::kThreads;  // chunks per thread
+        constexpr int kRowStep = C::kThreads / 16;
         const long long r0 = (long long)kb * C::kBk;
-        // 1. dequantize the block's K and V rows (rows past L repeat row L - 1:
-        //    masked, weight 0)
-        {
-            // thread tid takes chunk c = tid % 16 of rows tid / 16 + 16 t: one
-            // base row per block, the rest constant offsets (rows 16 apart keep
-            // the swizzle phase, so the shared-memory offsets are constant too)
-            constexpr int kPer = C::kBk * 16 / C::kThreads;  // chunks per thread
-            constexpr int kRowStep = C::kThreads / 16;
-            const int c = tid & 15, rr = tid >> 4;
-            PfRaw<C::kKind> rk[kPer], rv[kPer];
-            if (r0 + C::kBk <= p.L) {
-                const long long grow = (long long)hk * p.L + r0 + rr;
+        const int c = tid & 15, rr = tid >> 4;
+        PfRaw<C::kKind> raw[kPer];
+        if (r0 + C::kBk <= p.L) {
+            const long long grow = (long long)hk * p.L + r0 + rr;
 #pragma unroll
-                for (int t = 0; t < kPer; ++t) {
-                    rk[t] = pf_load<C::kKind>(p.K, p.scK, grow + kRowStep * t, c);
-                    rv[t] = pf_load<C::kKind>(p.V, p.scV, grow + kRowStep * t, c);
-                }
-            } else {  // the cache's last block: rows past L repeat row L - 1 (masked, weight 0)
-#pragma unroll
-                for (int t = 0; t < kPer; ++t) {
-                    const long long grow = (long long)hk * p.L + min(r0 + rr + kRowStep * t, (long long)p.L - 1);
-                    rk[t] = pf_load<C::kKind>(p.K, p.scK, grow, c);
-                    rv[t] = pf_load<C::kKind>(p.V, p.scV, grow, c);
-                }
-            }
-            const uint32_t so = pf_off(rr, c);
+            for (int t = 0; t < kPer; ++t) raw[t] = pf_load<C::kKind>(codes, scales, grow + kRowStep * t, c);
+        } else {  // the cache's last block: rows past L repeat row L - 1 (masked, weight 0)
 #pragma unroll
             for (int t = 0; t < kPer; ++t) {
-                sts128_generic(sK, so + kRowStep * 128 * t, pf_convert<C::kKind>(rk[t]));
-                sts128_generic(sV, so + kRowStep * 128 * t, pf_convert<C::kKind>(rv[t]));
+                const long long grow = (long long)hk * p.L + min(r0 + rr + kRowStep * t, (long long)p.L - 1);
+                raw[t] = pf_load<C::kKind>(codes, scales, grow, c);
             }
         }
-        fence_proxy_async_smem();
-        tc05_fence_before();
-        __syncthreads();
-        // 2. S = Q K^T
+        const uint32_t so = pf_off(rr, c);
+#pragma unroll
+        for (int t = 0; t < kPer; ++t) sts128_generic(dst, so + kRowStep * 128 * t, pf_convert<C::kKind>(raw[t]));
+    };
+    const auto issue_s = [&]() {  // S = Q K^T of the block in the K tile
         if (tid == 0) {
             tc05_fence_after();
 #pragma unroll
@@ -421,6 +410,18 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             }
             umma_commit(bar_s);
         }
+    };
+    // Schedule per block kb: wait S(kb); softmax; issue PV(kb); dequantize
+    // K(kb+1) while PV(kb) runs (S(kb) has read K); wait PV(kb); issue
+    // S(kb+1); dequantize V(kb+1) while S(kb+1) runs (PV(kb) has read V).
+    dequant(0, p.K, p.scK, sK);
+    dequant(0, p.V, p.scV, sV);
+    fence_proxy_async_smem();
+    tc05_fence_before();
+    __syncthreads();
+    issue_s();
+    for (int kb = 0; kb < nkb; ++kb) {
+        const long long r0 = (long long)kb * C::kBk;
         const bool ok_s = mbar_wait_bounded(bar_s, (uint32_t)kb & 1u);
         if (!ok_s && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
@@ -518,12 +519,20 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             }
             umma_commit(bar_o);
         }
+        const bool more = kb + 1 < nkb;
+        if (more) dequant(kb + 1, p.K, p.scK, sK);
         const bool ok_o = mbar_wait_bounded(bar_o, (uint32_t)kb & 1u);
         if (!ok_o && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
+        if (more) fence_proxy_async_smem();
         if (__syncthreads_or(!ok_o)) {
             if (tid == 0) *fail = 1;
             break;
+        }
+        if (more) {
+            issue_s();
+            dequant(kb + 1, p.V, p.scV, sV);
+            fence_proxy_async_smem();
         }
     }
     // epilogue: out = O / l for the CTA's valid tokens (l: both halves' sums)
