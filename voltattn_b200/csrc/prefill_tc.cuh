@@ -460,7 +460,13 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             xch[hf * 128 + row] = fmaxf(bm0, bm1);
             __syncthreads();
             const float bm = fmaxf(xch[row], xch[128 + row]);
-            const float mnew = fmaxf(m, bm * qk_scale);
+            // the reference maximum moves only when the block's maximum exceeds
+            // it by more than 8 (log2 units): weights stay <= 256, exact in
+            // relative terms in fp16, and O is rarely rescaled. O and l share
+            // the reference, so the result is the same. Both halves of a row
+            // take the same decision (same m, same exchanged maximum).
+            const float bms = bm * qk_scale;
+            const float mnew = bms > m + 8.f ? bms : m;
             const float corr = fast_exp2(m - mnew);
             m = mnew;
             float2 sum2 = make_float2(0.f, 0.f);
