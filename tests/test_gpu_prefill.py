@@ -32,6 +32,8 @@ CASES = [  # fmt, Hq, Hkv, L, Lq
     ("f16", 2, 2, 333, 77),
     ("q8", 2, 1, 1500, 200),
     ("q4+", 2, 2, 2049, 640),  # several token blocks, cache blocks past the diagonal
+    ("bf16+", 4, 2, 600, 200),
+    ("f8+", 4, 1, 777, 300),
 ]
 
 
@@ -40,6 +42,14 @@ def cache_for(oracle, fmt, kx, vx, rows, D):
     if fmt.startswith("f16"):
         kb, vb = oracle.f2h(kx), oracle.f2h(vx)
         return kb, vb, None, None, oracle.round_to_half(kx), oracle.round_to_half(vx)
+    if fmt == "bf16+":
+        kb, vb = oracle.f2bf(kx), oracle.f2bf(vx)
+        val = lambda b: (b.astype(np.uint32) << 16).view(np.float32)
+        return kb, vb, None, None, val(kb), val(vb)
+    if fmt == "f8+":
+        kc, ks = oracle.quantize_f8(kx, 1, rows, D)
+        vc, vs = oracle.quantize_f8(vx, 1, rows, D)
+        return kc, vc, ks, vs, oracle.dequant_f8(kc, ks, 1, rows, D), oracle.dequant_f8(vc, vs, 1, rows, D)
     bits = BITS[fmt]
     kc, ks = oracle.quantize(kx, 1, rows, D, bits)
     vc, vs = oracle.quantize(vx, 1, rows, D, bits)
@@ -90,5 +100,5 @@ def test_prefill_rejects_unsupported(va):
         va.prefill("q4+", b, Hq, Hkv, L, Lq, 64)
     with pytest.raises(RuntimeError):  # more new tokens than cache rows
         va.prefill("q4+", b, Hq, Hkv, 4, Lq, 128)
-    with pytest.raises(RuntimeError):  # bf16+ has no prefill
-        va.prefill("bf16+", b, Hq, Hkv, L, Lq, 128)
+    with pytest.raises(RuntimeError):  # q4c+ has no prefill
+        va.prefill("q4c+", b, Hq, Hkv, L, Lq, 128)

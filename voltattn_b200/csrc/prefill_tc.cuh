@@ -35,6 +35,8 @@
 // transpose. Every wait on an mbarrier is bounded.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "formats.cuh"
 
@@ -62,7 +64,9 @@ struct PrefillCfg {
     // Q, K, V + barriers and the row-max exchange: 100 KB, 2 CTAs per SM
     static constexpr int kSmemBytes = 1024 + 3 * kTile + 64 + 2 * kBq * 4;  // + row-max exchange
     static constexpr int kTmemCols = 256;  // S and O, 128 fp32 columns each (2 CTAs: all 512)
-    static_assert(K == Kind::F16 || K == Kind::Q8 || K == Kind::Q4 || K == Kind::Q3, "fp16 or integer codes");
+    static_assert(K == Kind::F16 || K == Kind::BF16 || K == Kind::F8 || K == Kind::Q8 || K == Kind::Q4 ||
+                      K == Kind::Q3,
+                  "16-bit rows, fp8 or integer codes");
     static_assert((kThreads / 16) % 8 == 0, "dequant rows of a thread share the swizzle phase");
 };
 
@@ -239,7 +243,7 @@ __device__ __forceinline__ uint32_t pf_h2(uint32_t bytes, uint32_t sel, __half2 
 // compiler will not move loads across).
 template <Kind K>
 struct PfRaw {
-    uint32_t w[K == Kind::F16 ? 4 : K == Kind::Q8 ? 2 : 1];
+    uint32_t w[(K == Kind::F16 || K == Kind::BF16) ? 4 : (K == Kind::Q8 || K == Kind::F8) ? 2 : 1];
     __half sc;
 };
 
@@ -248,7 +252,7 @@ __device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* 
     constexpr int kRb = PrefillCfg<K>::kRb;
     const uint8_t* src = codes + (size_t)row * kRb;
     PfRaw<K> r;
-    if constexpr (K == Kind::F16) {
+    if constexpr (K == Kind::F16 || K == Kind::BF16) {
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + c);
         r.w[0] = v.x;
         r.w[1] = v.y;
@@ -257,7 +261,7 @@ __device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* 
         r.sc = __float2half(0.f);
     } else {
         r.sc = __ldg(scales + (size_t)row * 2 + (c >> 3));
-        if constexpr (K == Kind::Q8) {
+        if constexpr (K == Kind::Q8 || K == Kind::F8) {
             const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + c);
             r.w[0] = v.x;
             r.w[1] = v.y;
@@ -276,6 +280,29 @@ template <Kind K>
 __device__ __forceinline__ uint4 pf_convert(const PfRaw<K>& raw) {
     if constexpr (K == Kind::F16) {
         return make_uint4(raw.w[0], raw.w[1], raw.w[2], raw.w[3]);
+    } else if constexpr (K == Kind::BF16) {
+        // bf16 -> fp16: exact for values inside fp16's range (fp16 has the
+        // longer mantissa); bf16 rows beyond it saturate to infinity
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.w[i]));
+            const __half2 h = __float22half2_rn(f);
+            o[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        return make_uint4(o[0], o[1], o[2], o[3]);
+    } else if constexpr (K == Kind::F8) {
+        // e4m3 pairs -> fp16 (exact), then the group scale with one rounding
+        const __half2 sc = __half2half2(raw.sc);
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2_raw hr =
+                __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(raw.w[i >> 1] >> (16 * (i & 1))), __NV_E4M3);
+            const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&hr), sc);
+            o[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        return make_uint4(o[0], o[1], o[2], o[3]);
     } else {
         const __half2 sc = __half2half2(raw.sc);
         uint4 r;
