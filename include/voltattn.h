@@ -213,11 +213,10 @@ VA_API int va_append_kv(int bits, const float* x, void* codes, void* scales, int
 /* Prefill: attention of Lq new tokens of one sequence over its cache (no
  * reference counterpart; the reference decodes one token at a time). The
  * tokens' K/V rows are already in the cache as its last Lq rows: K/V
- * [Hkv][L] rows in format fmt (f16, f16+, bf16+, f8+, q8, q8+, q4, q4+, q3+;
- * scales [Hkv][L][D/64]). Token i (0 <= i < Lq) of query head h attends to
- * rows [0, L - Lq + i] of KV head h / (Hq/Hkv). q, out: __half [Hq][Lq][D],
- * 16-byte aligned. D = 128 (else VA_ERR_UNSUPPORTED); q4c+ returns
- * VA_ERR_UNSUPPORTED. Runs on the tcgen05 tensor cores with the
+ * [Hkv][L] rows in any format (scales [Hkv][L][D/64]; q4c+: K channel scales
+ * [Hkv][D], V row scales [Hkv][L]). Token i (0 <= i < Lq) of query head h
+ * attends to rows [0, L - Lq + i] of KV head h / (Hq/Hkv). q, out: __half
+ * [Hq][Lq][D], 16-byte aligned. D = 128 (else VA_ERR_UNSUPPORTED). Runs on the tcgen05 tensor cores with the
  * cache dequantized to fp16 tile by tile. */
 VA_API int va_prefill(int fmt, const va_bufs* bufs, int Hq, int Hkv, int L, int Lq, int D, void* stream);
 

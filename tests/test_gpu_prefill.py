@@ -34,10 +34,11 @@ CASES = [  # fmt, Hq, Hkv, L, Lq
     ("q4+", 2, 2, 2049, 640),  # several token blocks, cache blocks past the diagonal
     ("bf16+", 4, 2, 600, 200),
     ("f8+", 4, 1, 777, 300),
+    ("q4c+", 8, 2, 900, 260),  # per-channel K scales, per-row V scales
 ]
 
 
-def cache_for(oracle, fmt, kx, vx, rows, D):
+def cache_for(oracle, fmt, kx, vx, rows, D, L):
     """Device-side codes and scales plus the exact values the reference attends over."""
     if fmt.startswith("f16"):
         kb, vb = oracle.f2h(kx), oracle.f2h(vx)
@@ -46,6 +47,11 @@ def cache_for(oracle, fmt, kx, vx, rows, D):
         kb, vb = oracle.f2bf(kx), oracle.f2bf(vx)
         val = lambda b: (b.astype(np.uint32) << 16).view(np.float32)
         return kb, vb, None, None, val(kb), val(vb)
+    if fmt == "q4c+":  # K scales per (KV head, channel), V scales per row
+        H = rows // L
+        kc, ks = oracle.quantize_kchan(kx, H, L, D, 4)
+        vc, vs = oracle.quantize_vtok(vx, H, L, D, 4)
+        return kc, vc, ks, vs, oracle.dequant_kchan(kc, ks, H, L, D, 4), oracle.dequant_vtok(vc, vs, H, L, D, 4)
     if fmt == "f8+":
         kc, ks = oracle.quantize_f8(kx, 1, rows, D)
         vc, vs = oracle.quantize_f8(vx, 1, rows, D)
@@ -64,7 +70,7 @@ def test_prefill(va, oracle, case):
     rng = np.random.default_rng(Hq * 131 + Hkv * 17 + L + Lq)
     rows = Hkv * L
     kx, vx, _ = oracle.gen_case(int(rng.integers(1 << 30)), 1, rows, D)
-    kc, vc, ks, vs, kd, vd = cache_for(oracle, fmt, kx, vx, rows, D)
+    kc, vc, ks, vs, kd, vd = cache_for(oracle, fmt, kx, vx, rows, D, L)
     q = oracle.f2h(rng.standard_normal(Hq * Lq * D).astype(np.float32)).reshape(Hq, Lq, D)
     ref = np.empty((Hq, Lq, D), np.float32)
     for i in range(Lq):
@@ -100,5 +106,3 @@ def test_prefill_rejects_unsupported(va):
         va.prefill("q4+", b, Hq, Hkv, L, Lq, 64)
     with pytest.raises(RuntimeError):  # more new tokens than cache rows
         va.prefill("q4+", b, Hq, Hkv, 4, Lq, 128)
-    with pytest.raises(RuntimeError):  # q4c+ has no prefill
-        va.prefill("q4c+", b, Hq, Hkv, L, Lq, 128)

@@ -37,6 +37,8 @@
 
 #include <cuda_bf16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "formats.cuh"
 
@@ -52,9 +54,12 @@ struct PrefillParams {
     int Hq, Hkv, L, Lq;
 };
 
-template <Kind K>
+// kChanScales: the q4c+ layout, K codes with per-channel scales per KV head
+// ([Hkv][D]) and V codes with one scale per row ([Hkv][L]).
+template <Kind K, bool kChanScales = false>
 struct PrefillCfg {
     static constexpr Kind kKind = K;
+    static constexpr bool kChan = kChanScales;
     static constexpr int kD = 128;
     static constexpr int kBq = 128;  // tokens per CTA (MMA M)
     static constexpr int kBk = 128;  // cache rows per block (MMA N of S, K of O)
@@ -67,6 +72,7 @@ struct PrefillCfg {
     static_assert(K == Kind::F16 || K == Kind::BF16 || K == Kind::F8 || K == Kind::Q8 || K == Kind::Q4 ||
                       K == Kind::Q3,
                   "16-bit rows, fp8 or integer codes");
+    static_assert(!kChan || K == Kind::Q4, "per-channel / per-row scales: q4 codes");
     static_assert((kThreads / 16) % 8 == 0, "dequant rows of a thread share the swizzle phase");
 };
 
@@ -247,7 +253,9 @@ struct PfRaw {
     __half sc;
 };
 
-template <Kind K>
+// kScale: 0 = fp16 scales per 64-element group ([rows][2]), 1 = one scale per
+// row ([rows]), 2 = none loaded (per-channel scales, applied by the caller).
+template <Kind K, int kScale = 0>
 __device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* scales, long long row, int c) {
     constexpr int kRb = PrefillCfg<K>::kRb;
     const uint8_t* src = codes + (size_t)row * kRb;
@@ -260,7 +268,9 @@ __device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* 
         r.w[3] = v.w;
         r.sc = __float2half(0.f);
     } else {
-        r.sc = __ldg(scales + (size_t)row * 2 + (c >> 3));
+        if constexpr (kScale == 0) r.sc = __ldg(scales + (size_t)row * 2 + (c >> 3));
+        else if constexpr (kScale == 1) r.sc = __ldg(scales + (size_t)row);
+        else r.sc = __float2half(1.f);
         if constexpr (K == Kind::Q8 || K == Kind::F8) {
             const uint2 v = __ldg(reinterpret_cast<const uint2*>(src) + c);
             r.w[0] = v.x;
@@ -340,6 +350,15 @@ __device__ __forceinline__ uint4 pf_convert(const PfRaw<K>& raw) {
     }
 }
 
+// q4 chunk with a scale per dim pair (per-channel K scales of the chunk's 8 dims).
+__device__ __forceinline__ uint4 pf_convert_q4_chan(uint32_t w, const __half2* sc4) {
+    const __half2 off = __float2half2_rn(1032.f);
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+    const uint32_t p01 = __byte_perm(lo, hi, 0x5140), p23 = __byte_perm(lo, hi, 0x7362);
+    return make_uint4(pf_h2(p01, 0x4140, off, sc4[0]), pf_h2(p01, 0x4342, off, sc4[1]), pf_h2(p23, 0x4140, off, sc4[2]),
+                      pf_h2(p23, 0x4342, off, sc4[3]));
+}
+
 __device__ __forceinline__ void sts128_generic(uint8_t* base, uint32_t off, uint4 v) {
     *reinterpret_cast<uint4*>(base + off) = v;
 }
@@ -405,7 +424,16 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     // tid takes chunk c = tid % 16 of rows tid / 16 + 16 t: one base row per
     // block, the rest constant offsets (rows 16 apart keep the swizzle phase,
     // so the shared-memory offsets are constant too). All loads go out first.
-    const auto dequant = [&](int kb, const uint8_t* codes, const __half* scales, uint8_t* dst) {
+    // q4c+: this thread's 8 dims (chunk tid % 16) of the KV head's channel scales
+    __half2 kcs[4];
+    if constexpr (C::kChan) {
+        const __half* cs = p.scK + (size_t)hk * D + 8 * (tid & 15);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) kcs[i] = __halves2half2(__ldg(cs + 2 * i), __ldg(cs + 2 * i + 1));
+    }
+    const auto dequant = [&](auto is_k, int kb, const uint8_t* codes, const __half* scales, uint8_t* dst) {
+        // scale layout of this matrix: groups, or q4c+ channels (K) / rows (V)
+        constexpr int kScale = !C::kChan ? 0 : decltype(is_k)::value ? 2 : 1;
         constexpr int kPer = C::kBk * 16 / C::kThreads;  // chunks per thread
         constexpr int kRowStep = C::kThreads / 16;
         const long long r0 = (long long)kb * C::kBk;
@@ -414,17 +442,22 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         if (r0 + C::kBk <= p.L) {
             const long long grow = (long long)hk * p.L + r0 + rr;
 #pragma unroll
-            for (int t = 0; t < kPer; ++t) raw[t] = pf_load<C::kKind>(codes, scales, grow + kRowStep * t, c);
+            for (int t = 0; t < kPer; ++t) raw[t] = pf_load<C::kKind, kScale>(codes, scales, grow + kRowStep * t, c);
         } else {  // the cache's last block: rows past L repeat row L - 1 (masked, weight 0)
 #pragma unroll
             for (int t = 0; t < kPer; ++t) {
                 const long long grow = (long long)hk * p.L + min(r0 + rr + kRowStep * t, (long long)p.L - 1);
-                raw[t] = pf_load<C::kKind>(codes, scales, grow, c);
+                raw[t] = pf_load<C::kKind, kScale>(codes, scales, grow, c);
             }
         }
         const uint32_t so = pf_off(rr, c);
 #pragma unroll
-        for (int t = 0; t < kPer; ++t) sts128_generic(dst, so + kRowStep * 128 * t, pf_convert<C::kKind>(raw[t]));
+        for (int t = 0; t < kPer; ++t) {
+            if constexpr (kScale == 2)
+                sts128_generic(dst, so + kRowStep * 128 * t, pf_convert_q4_chan(raw[t].w[0], kcs));
+            else
+                sts128_generic(dst, so + kRowStep * 128 * t, pf_convert<C::kKind>(raw[t]));
+        }
     };
     const auto issue_s = [&]() {  // S = Q K^T of the block in the K tile
         if (tid == 0) {
@@ -441,8 +474,10 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
     // Schedule per block kb: wait S(kb); softmax; issue PV(kb); dequantize
     // K(kb+1) while PV(kb) runs (S(kb) has read K); wait PV(kb); issue
     // S(kb+1); dequantize V(kb+1) while S(kb+1) runs (PV(kb) has read V).
-    dequant(0, p.K, p.scK, sK);
-    dequant(0, p.V, p.scV, sV);
+    using kIsK = std::integral_constant<bool, true>;
+    using kIsV = std::integral_constant<bool, false>;
+    dequant(kIsK{}, 0, p.K, p.scK, sK);
+    dequant(kIsV{}, 0, p.V, p.scV, sV);
     fence_proxy_async_smem();
     tc05_fence_before();
     __syncthreads();
@@ -553,7 +588,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             umma_commit(bar_o);
         }
         const bool more = kb + 1 < nkb;
-        if (more) dequant(kb + 1, p.K, p.scK, sK);
+        if (more) dequant(kIsK{}, kb + 1, p.K, p.scK, sK);
         const bool ok_o = mbar_wait_bounded(bar_o, (uint32_t)kb & 1u);
         if (!ok_o && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
@@ -564,7 +599,7 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         }
         if (more) {
             issue_s();
-            dequant(kb + 1, p.V, p.scV, sV);
+            dequant(kIsV{}, kb + 1, p.V, p.scV, sV);
             fence_proxy_async_smem();
         }
     }

@@ -1020,7 +1020,6 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
     if (!is_valid_fmt(fmt) || !b) return VA_ERR_INVALID;
     if (Hq < 1 || Hkv < 1 || Hq % Hkv || Lq < 1 || L < Lq) return VA_ERR_INVALID;
     if (D != 128) return VA_ERR_UNSUPPORTED;
-    if (fmt == VA_Q4CP) return VA_ERR_UNSUPPORTED;
     if (Hq > 65535 || (long long)Hkv * L >= (1ll << 40)) return VA_ERR_TOO_LARGE;
     if (!b->K || !b->V || !b->q || !b->out) return VA_ERR_INVALID;
     if (!is_f16(fmt) && (!b->scK || !b->scV)) return VA_ERR_INVALID;
@@ -1040,6 +1039,7 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
     p.Lq = Lq;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (fmt == VA_BF16P) return launch_prefill<PrefillCfg<Kind::BF16>>(p, st);
+    if (fmt == VA_Q4CP) return launch_prefill<PrefillCfg<Kind::Q4, true>>(p, st);
     if (fmt == VA_F8P) return launch_prefill<PrefillCfg<Kind::F8>>(p, st);
     switch (fmt_bits(fmt)) {
         case 16: return launch_prefill<PrefillCfg<Kind::F16>>(p, st);
