@@ -328,11 +328,11 @@ def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, spli
 
 
 def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
-    """End to end through the public API, as a serving loop runs it: one decode
-    step (H2D of this step's q from pinned host memory, va.launch, D2H of the fp16
-    output into pinned host memory) captured once as a CUDA graph per cache copy;
-    per step the host writes q into the pinned buffer, replays the graph and
-    synchronizes the stream. Caches rotate over > 4x L2 so every decode reads HBM."""
+    """End to end through the public API, as a serving loop runs it: per step
+    the host writes this step's q into pinned memory and calls va_decode_host
+    (H2D of q, the decode, D2H of the fp16 output into pinned memory; a cached
+    CUDA graph per cache copy; returns synchronized), then reads the output.
+    Caches rotate over > 4x L2 so every decode reads HBM."""
     import math
     nbytes = algorithmic_bytes(fmt, L)
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
@@ -351,40 +351,22 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     stream = torch.cuda.Stream(device=dev)
     bufs = [va.DeviceBufs(*c, q, out, ws) for c in caches]
 
-    def body(bb):
-        # 8 KB each way: the pinned buffers are device-mapped, so a small copy
-        # kernel moves them (a copy-engine transfer costs ~6 us of latency here)
-        va.copy_small(q, q_pin, stream)
-        va.launch(fmt, bb, H, L, D, S, stream)
-        va.copy_small(out_pin, out, stream)
-
-    with torch.cuda.stream(stream):
-        for bb in bufs:  # warm-up outside capture (workspace, tensor-map encoder)
-            body(bb)
-    stream.synchronize()
-    graphs = []
-    for bb in bufs:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            body(bb)
-        graphs.append(g)
-    steps = min(K_steps, 20000)
-
     # host side through numpy views of the pinned buffers (cheaper than torch ops)
     q_src_np, q_pin_np = q_src.numpy(), q_pin.numpy()
     out_pin_np, out_sink_np = out_pin.numpy(), out_sink.numpy()
+    steps = min(K_steps, 20000)
+
+    # va_decode_host per cache copy with its arguments bound once (va.HostStep):
+    # q from pinned memory, decode, output to pinned memory, synchronized; a
+    # cached CUDA graph after the first call
+    host_steps = [va.HostStep(fmt, bb, q_pin, out_pin, H, L, D, S, stream) for bb in bufs]
 
     def one(i):
         q_pin_np[:] = q_src_np[i % nq]
-        graphs[i % copies].replay()  # on the current stream: `stream`, set once below
-        stream.synchronize()
+        host_steps[i % copies]()
         out_sink_np[i % nq] = out_pin_np
 
-    # the serving loop's stream is made current once: a `with torch.cuda.stream`
-    # block per step costs ~6 us of Python, a third of the decode
-    prev_stream = torch.cuda.current_stream(dev)
-    torch.cuda.set_stream(stream)
-    for i in range(5):
+    for i in range(2 * copies):  # every copy's first call captures its graph
         one(i)
     if dist:
         dist.barrier()
@@ -392,7 +374,6 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     for i in range(steps):
         one(i)
     dt = time.perf_counter() - t0
-    torch.cuda.set_stream(prev_stream)
     if dist:
         t = torch.tensor([dt], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -401,8 +382,8 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     return {"value": n * steps / dt, "unit": "tok/s", "h2d_bytes_per_step": H * D * 2,
             "d2h_bytes_per_step": H * D * 2, "steps": steps,
             "note": "KV cache resident in HBM (decode state), rotating over > 4x L2; per step: q written to "
-                    "pinned memory, one CUDA graph (H2D q, decode, D2H output; the transfers by va_copy_small from / "
-                    "to device-mapped pinned memory) replayed, stream synchronized"}
+                    "pinned memory, va_decode_host (H2D q, decode, D2H output by va_copy_small from / to "
+                    "device-mapped pinned memory, as one cached CUDA graph; returns synchronized), output read"}
 
 
 def make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S):

@@ -198,6 +198,19 @@ VA_API int va_quantize_vtok(int bits, const float* x, void* codes, void* scales,
  * out without a copy-engine transfer (no reference counterpart). */
 VA_API int va_copy_small(void* dst, const void* src, size_t bytes, void* stream);
 
+/* One decode step with the query and the output in pinned host memory (no
+ * reference counterpart; the reference's launch takes device buffers only):
+ * copies q_host [H][D] fp16 into bufs->q, runs va_decode, copies bufs->out into
+ * out_host, and returns once out_host holds the result (it synchronizes the
+ * stream). Arguments as for va_decode; q_host, out_host, bufs->q and bufs->out
+ * 16-byte aligned. On a created stream the three launches are captured into a
+ * CUDA graph on the first call with a given argument set and replayed on later
+ * calls with the same set (up to 16 sets cached, oldest dropped). The first
+ * call therefore captures: make it outside any other stream capture. On the
+ * legacy default stream (stream = NULL) the launches are made directly. */
+VA_API int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_host, int H, int L, int D,
+                          int S, void* ws, size_t ws_bytes, void* stream);
+
 /* KV append for decode loops (no reference counterpart; the reference
  * quantizes a whole cache once). Quantizes one new row per KV head of each
  * sequence, x = fp32 [B][Hkv][D], into a cache laid out as for

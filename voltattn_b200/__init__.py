@@ -66,6 +66,8 @@ def _load():
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
     lib.va_copy_small.argtypes = [vp, vp, sz, vp]; lib.va_copy_small.restype = i
+    lib.va_decode_host.argtypes = [i, C.POINTER(VaBufs), vp, vp, i, i, i, i, vp, sz, vp]
+    lib.va_decode_host.restype = i
     for fn in ("va_quantize_kchan", "va_quantize_vtok"):
         getattr(lib, fn).argtypes = [i, vp, vp, vp, i, i, i, vp]
         getattr(lib, fn).restype = i
@@ -252,6 +254,34 @@ def copy_small(dst, src, stream=None):
     nbytes = src.numel() * src.element_size()
     assert dst.numel() * dst.element_size() == nbytes
     _check(_lib.va_copy_small(_ptr(dst), _ptr(src), nbytes, _stream_ptr(stream)), "copy_small")
+
+
+def decode_host(fmt, b: DeviceBufs, q_host, out_host, H: int, L: int, D: int, S: int, stream=None):
+    """One decode step with q and out in pinned host memory (va_decode_host):
+    q_host -> b.q, decode, b.out -> out_host; returns once out_host holds the
+    output. On a created stream the step is a cached CUDA graph after its first
+    call with these arguments."""
+    vb = b.va()
+    _check(_lib.va_decode_host(int(Fmt.parse(fmt)), C.byref(vb), _ptr(q_host), _ptr(out_host), H, L, D, S,
+                               _ptr(b.ws), b.ws.numel() * b.ws.element_size(), _stream_ptr(stream)), "decode_host")
+
+
+class HostStep:
+    """decode_host with its arguments bound once, for serving loops: calling
+    the object runs one step (one C call; the tensors must stay alive and in
+    place, as for the captured graph behind it)."""
+
+    def __init__(self, fmt, b: DeviceBufs, q_host, out_host, H: int, L: int, D: int, S: int, stream=None):
+        self._keep = (b, q_host, out_host, stream)
+        self._vb = b.va()
+        self._args = (int(Fmt.parse(fmt)), C.byref(self._vb), _ptr(q_host), _ptr(out_host), H, L, D, S,
+                      _ptr(b.ws), b.ws.numel() * b.ws.element_size(), _stream_ptr(stream))
+        self._fn = _lib.va_decode_host
+
+    def __call__(self):
+        rc = self._fn(*self._args)
+        if rc:
+            _check(rc, "decode_host")
 
 
 def quantize_f8(x, H: int, L: int, D: int, codes=None, scales=None, stream=None):

@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include <cudaTypedefs.h>
 
@@ -542,6 +543,25 @@ int launch_prefill(const PrefillParams& p, cudaStream_t st) {
     return VA_OK;
 }
 
+// ---- decode with host-side q / out: one cached CUDA graph per argument set ----
+struct HostStepKey {
+    int dev, fmt, H, L, D, S;
+    va_bufs b;
+    const void* q_host;
+    void* out_host;
+    void* ws;
+    size_t ws_bytes;
+    cudaStream_t st;
+    bool operator==(const HostStepKey& o) const { return std::memcmp(this, &o, sizeof(*this)) == 0; }
+};
+struct HostStepGraph {
+    HostStepKey key;
+    cudaGraphExec_t exec;
+};
+constexpr size_t kHostStepGraphs = 16;  // cached graphs (oldest evicted)
+std::mutex g_host_step_mu;
+std::vector<HostStepGraph> g_host_steps;
+
 extern "C" {
 
 int va_version(void) { return 100; }
@@ -1047,6 +1067,78 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
         case 4: return launch_prefill<PrefillCfg<Kind::Q4>>(p, st);
         default: return launch_prefill<PrefillCfg<Kind::Q3>>(p, st);
     }
+}
+
+int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_host, int H, int L, int D, int S,
+                   void* ws, size_t ws_bytes, void* stream) {
+    int rc = check_decode_args(fmt, bufs, H, L, D, S);
+    if (rc) return rc;
+    if (!q_host || !out_host) return VA_ERR_INVALID;
+    if (!aligned16(q_host) || !aligned16(out_host) || !aligned16(bufs->q) || !aligned16(bufs->out))
+        return VA_ERR_ALIGN;
+    const size_t bytes = (size_t)H * D * sizeof(__half);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const auto step = [&]() -> int {
+        int r = va_copy_small(const_cast<void*>(bufs->q), q_host, bytes, st);
+        if (!r) r = decode_impl(fmt, bufs, H, L, D, S, ws, ws_bytes, nullptr, st);
+        if (!r) r = va_copy_small(out_host, bufs->out, bytes, st);
+        return r;
+    };
+    if (!st) {  // the legacy default stream cannot be captured: direct launches
+        rc = step();
+        if (rc) return rc;
+        VA_CUDA(cudaStreamSynchronize(st));
+        return VA_OK;
+    }
+    HostStepKey key;
+    std::memset(&key, 0, sizeof(key));
+    rc = current_device(&key.dev);
+    if (rc) return rc;
+    key.fmt = fmt;
+    key.H = H;
+    key.L = L;
+    key.D = D;
+    key.S = S;
+    key.b = *bufs;
+    key.q_host = q_host;
+    key.out_host = out_host;
+    key.ws = ws;
+    key.ws_bytes = ws_bytes;
+    key.st = st;
+    cudaGraphExec_t exec = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_host_step_mu);
+        for (const auto& g : g_host_steps)
+            if (g.key == key) exec = g.exec;
+    }
+    if (exec) {
+        VA_CUDA(cudaGraphLaunch(exec, st));
+        VA_CUDA(cudaStreamSynchronize(st));
+        return VA_OK;
+    }
+    // first call with these arguments: run directly (also the warm-up of the
+    // decode's one-time set-up), then capture the same three launches
+    rc = step();
+    if (rc) return rc;
+    VA_CUDA(cudaStreamSynchronize(st));
+    cudaGraph_t graph = nullptr;
+    VA_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const int rc_cap = step();
+    const cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc_cap || e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc_cap ? rc_cap : VA_ERR_CUDA;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) return VA_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_host_step_mu);
+    if (g_host_steps.size() >= kHostStepGraphs) {
+        cudaGraphExecDestroy(g_host_steps.front().exec);
+        g_host_steps.erase(g_host_steps.begin());
+    }
+    g_host_steps.push_back(HostStepGraph{key, exec});
+    return VA_OK;
 }
 
 int va_device_error(int* code) {
