@@ -330,7 +330,7 @@ def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, spli
 def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     """End to end through the public API, as a serving loop runs it: per step
     the host writes this step's q into pinned memory and calls va_decode_host
-    (H2D of q, the decode, D2H of the fp16 output into pinned memory; a cached
+    (H2D of q, the decode storing its fp16 output into pinned memory; a cached
     CUDA graph per cache copy; returns synchronized), then reads the output.
     Caches rotate over > 4x L2 so every decode reads HBM."""
     import math
@@ -382,8 +382,9 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     return {"value": n * steps / dt, "unit": "tok/s", "h2d_bytes_per_step": H * D * 2,
             "d2h_bytes_per_step": H * D * 2, "steps": steps,
             "note": "KV cache resident in HBM (decode state), rotating over > 4x L2; per step: q written to "
-                    "pinned memory, va_decode_host (H2D q, decode, D2H output by va_copy_small from / to "
-                    "device-mapped pinned memory, as one cached CUDA graph; returns synchronized), output read"}
+                    "pinned memory, va_decode_host (H2D q by va_copy_small from device-mapped pinned memory, decode "
+                    "storing its output into pinned memory, as one cached CUDA graph; returns synchronized), "
+                    "output read"}
 
 
 def make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S):

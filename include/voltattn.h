@@ -200,10 +200,10 @@ VA_API int va_copy_small(void* dst, const void* src, size_t bytes, void* stream)
 
 /* One decode step with the query and the output in pinned host memory (no
  * reference counterpart; the reference's launch takes device buffers only):
- * copies q_host [H][D] fp16 into bufs->q, runs va_decode, copies bufs->out into
- * out_host, and returns once out_host holds the result (it synchronizes the
- * stream). Arguments as for va_decode; q_host, out_host, bufs->q and bufs->out
- * 16-byte aligned. On a created stream the three launches are captured into a
+ * copies q_host [H][D] fp16 into bufs->q, runs va_decode with its output
+ * stored straight into out_host (bufs->out is not used), and returns once
+ * out_host holds the result (it synchronizes the stream). Arguments as for
+ * va_decode; q_host, out_host and bufs->q 16-byte aligned. On a created stream the three launches are captured into a
  * CUDA graph on the first call with a given argument set and replayed on later
  * calls with the same set (up to 16 sets cached, oldest dropped). The first
  * call therefore captures: make it outside any other stream capture. On the

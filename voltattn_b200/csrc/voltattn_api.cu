@@ -1071,17 +1071,21 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
 
 int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_host, int H, int L, int D, int S,
                    void* ws, size_t ws_bytes, void* stream) {
-    int rc = check_decode_args(fmt, bufs, H, L, D, S);
+    if (!bufs || !q_host || !out_host) return VA_ERR_INVALID;
+    if (!aligned16(q_host) || !aligned16(out_host) || !aligned16(bufs->q)) return VA_ERR_ALIGN;
+    // the decode stores its output straight into out_host (mapped pinned
+    // memory takes plain global stores; the synchronize below makes them
+    // visible to the host); the query is copied in first, since the tile
+    // kernels bulk-copy it
+    va_bufs b2 = *bufs;
+    b2.out = out_host;
+    int rc = check_decode_args(fmt, &b2, H, L, D, S);
     if (rc) return rc;
-    if (!q_host || !out_host) return VA_ERR_INVALID;
-    if (!aligned16(q_host) || !aligned16(out_host) || !aligned16(bufs->q) || !aligned16(bufs->out))
-        return VA_ERR_ALIGN;
     const size_t bytes = (size_t)H * D * sizeof(__half);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const auto step = [&]() -> int {
         int r = va_copy_small(const_cast<void*>(bufs->q), q_host, bytes, st);
-        if (!r) r = decode_impl(fmt, bufs, H, L, D, S, ws, ws_bytes, nullptr, st);
-        if (!r) r = va_copy_small(out_host, bufs->out, bytes, st);
+        if (!r) r = decode_impl(fmt, &b2, H, L, D, S, ws, ws_bytes, nullptr, st);
         return r;
     };
     if (!st) {  // the legacy default stream cannot be captured: direct launches
