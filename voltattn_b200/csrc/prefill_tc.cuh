@@ -487,10 +487,8 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         const bool ok_s = mbar_wait_bounded(bar_s, (uint32_t)kb & 1u);
         if (!ok_s && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
-        if (__syncthreads_or(!ok_s)) {  // every thread leaves together
-            if (tid == 0) *fail = 1;
-            break;
-        }
+        // (a failed wait is agreed on at the row-max exchange below, the next
+        // CTA barrier; until then the thread only reads TMEM)
         // 3. online softmax of this thread's half token row; P -> sP; rescale O
         {
             // two passes over S in TMEM (the row maximum, then the weights).
@@ -520,7 +518,10 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
             }
             // the row's maximum over both halves
             xch[hf * 128 + row] = fmaxf(bm0, bm1);
-            __syncthreads();
+            if (__syncthreads_or(!ok_s)) {  // every thread leaves together
+                if (tid == 0) *fail = 1;
+                break;
+            }
             const float bm = fmaxf(xch[row], xch[128 + row]);
             // the reference maximum moves only when the block's maximum exceeds
             // it by more than 8 (log2 units): weights stay <= 256, exact in
