@@ -233,6 +233,16 @@ VA_API int va_append_kv(int bits, const float* x, void* codes, void* scales, int
  * cache dequantized to fp16 tile by tile. */
 VA_API int va_prefill(int fmt, const va_bufs* bufs, int Hq, int Hkv, int L, int Lq, int D, void* stream);
 
+/* va_prefill over a paged cache (no reference counterpart): the sequence's L
+ * rows (its last Lq the new tokens) live in the pool of va_decode_paged, row j
+ * of KV head k in page block_table[j / page_rows] (device int32 [max_pages],
+ * max_pages * page_rows >= L) at row j % page_rows of
+ * [num_pages][Hkv][page_rows] (scales alike). Entries outside [0, num_pages)
+ * read page 0. Any page_rows >= 1. Formats as va_prefill except q4c+
+ * (VA_ERR_UNSUPPORTED). */
+VA_API int va_prefill_paged(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, int page_rows,
+                            int num_pages, int Hq, int Hkv, int L, int Lq, int D, void* stream);
+
 /* Multi-query decode (no reference counterpart), e.g. verifying Q speculative
  * tokens: the Q new tokens of each sequence are already appended to the cache
  * ([B][Hkv][Lmax] rows as for va_decode_gqa, lens[b] counting them), and

@@ -106,3 +106,64 @@ def test_prefill_rejects_unsupported(va):
         va.prefill("q4+", b, Hq, Hkv, L, Lq, 64)
     with pytest.raises(RuntimeError):  # more new tokens than cache rows
         va.prefill("q4+", b, Hq, Hkv, 4, Lq, 128)
+
+
+PAGED = [  # fmt, Hq, Hkv, L, Lq, page_rows
+    ("q4+", 8, 2, 700, 300, 64),
+    ("q8+", 4, 4, 1000, 129, 48),   # pages not a multiple of the 128-row block
+    ("f16+", 2, 1, 513, 513, 256),
+    ("q3+", 4, 2, 400, 77, 32),
+]
+
+
+@pytest.mark.parametrize("case", PAGED, ids=lambda c: "{}_Hq{}_Hkv{}_L{}_Lq{}_P{}".format(*c))
+def test_prefill_paged(va, oracle, case):
+    """The contiguous case's cache scattered into a shuffled page pool whose
+    unused pages carry nan scales (or nan fp16 rows): the output must match
+    the oracle exactly as for the contiguous layout."""
+    import torch
+    fmt, Hq, Hkv, L, Lq, P = case
+    D = 128
+    rng = np.random.default_rng(Hq * 7 + L + P)
+    rows = Hkv * L
+    kx, vx, _ = oracle.gen_case(int(rng.integers(1 << 30)), 1, rows, D)
+    kc, vc, ks, vs, kd, vd = cache_for(oracle, fmt, kx, vx, rows, D, L)
+    q = oracle.f2h(rng.standard_normal(Hq * Lq * D).astype(np.float32)).reshape(Hq, Lq, D)
+    ref = np.empty((Hq, Lq, D), np.float32)
+    for i in range(Lq):
+        ref[:, i] = oracle.reference_gqa(kd, vd, np.ascontiguousarray(q[:, i]).ravel(),
+                                         np.array([L - Lq + 1 + i], np.int32), 1, Hq, Hkv, L, D).reshape(Hq, D)
+    max_pages = (L + P - 1) // P
+    num_pages = max_pages + 3
+    table = rng.permutation(num_pages)[:max_pages].astype(np.int32)
+
+    def scatter(arr, per_row, fill):
+        a = arr.reshape(Hkv, L, per_row)
+        pool = np.full((num_pages, Hkv, P, per_row), fill, arr.dtype)
+        for j in range(max_pages):
+            r1 = min((j + 1) * P, L)
+            pool[table[j], :, :r1 - j * P] = a[:, j * P:r1]
+        return pool.reshape(-1)
+
+    nan16 = np.uint16(0x7E00)
+    if fmt.startswith("f16"):
+        K, V = scatter(kc.view(np.uint16), D, nan16), scatter(vc.view(np.uint16), D, nan16)
+        sK = sV = None
+    else:
+        rb = kc.size // rows
+        K, V = scatter(kc, rb, 0), scatter(vc, rb, 0)
+        sK, sV = scatter(ks.view(np.uint16), 2, nan16), scatter(vs.view(np.uint16), 2, nan16)
+    as_dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    Kd, Vd = as_dev(K), as_dev(V)
+    sKd = None if sK is None else as_dev(sK).view(torch.float16)
+    sVd = None if sV is None else as_dev(sV).view(torch.float16)
+    qd = as_dev(q.ravel()).view(torch.float16)
+    out = torch.full((Hq * Lq * D,), float("nan"), dtype=torch.float16, device="cuda")
+    va.prefill_paged(fmt, va.DeviceBufs(Kd, Vd, sKd, sVd, qd, out), as_dev(table), max_pages, P, num_pages, Hq, Hkv,
+                     L, Lq, D)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy().reshape(Hq, Lq, D)
+    err = np.abs(got - ref)
+    bad = ~(err <= ATOL + RTOL * np.abs(ref))
+    assert not bad.any(), f"{case}: {bad.sum()} bad, maxerr {np.nanmax(err):.3e}"
+    assert va.device_error() == 0

@@ -75,6 +75,8 @@ def _load():
     lib.va_decode_multiquery.restype = i
     lib.va_prefill.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, i, vp]
     lib.va_prefill.restype = i
+    lib.va_prefill_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, i, vp]
+    lib.va_prefill_paged.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
     lib.va_decode_paged.restype = i
     lib.va_append_kv_paged.argtypes = [i, vp, vp, vp, vp, i, i, i, i, i, i, vp, vp]
@@ -341,6 +343,15 @@ def prefill(fmt, b: DeviceBufs, Hq: int, Hkv: int, L: int, Lq: int, D: int, stre
     [Hq][Lq][D]; b.ws unused."""
     vb = b.va()
     _check(_lib.va_prefill(int(Fmt.parse(fmt)), C.byref(vb), Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill")
+
+
+def prefill_paged(fmt, b: DeviceBufs, block_table, max_pages: int, page_rows: int, num_pages: int, Hq: int,
+                  Hkv: int, L: int, Lq: int, D: int, stream=None):
+    """prefill over a paged cache: b.K / b.V (and scales) are the page pool
+    [num_pages][Hkv][page_rows], block_table int32 [max_pages] (CUDA)."""
+    vb = b.va()
+    _check(_lib.va_prefill_paged(int(Fmt.parse(fmt)), C.byref(vb), _ptr(block_table), max_pages, page_rows, num_pages,
+                                 Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill_paged")
 
 
 def decode_paged(fmt, b: DeviceBufs, block_table, max_pages: int, lens, B: int, Hq: int, Hkv: int, page_rows: int,

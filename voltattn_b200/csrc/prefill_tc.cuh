@@ -52,6 +52,12 @@ struct PrefillParams {
     const __half* q;
     __half* out;
     int Hq, Hkv, L, Lq;
+    // paged cache (page_rows > 0): row j of KV head k lives in page
+    // block_table[j / page_rows] at physical row (page * Hkv + k) * page_rows +
+    // j % page_rows of [num_pages][Hkv][page_rows]; entries outside the pool
+    // read page 0
+    const int* block_table;
+    int page_rows, num_pages;
 };
 
 // kChanScales: the q4c+ layout, K codes with per-channel scales per KV head
@@ -363,7 +369,7 @@ __device__ __forceinline__ void sts128_generic(uint8_t* base, uint32_t off, uint
     *reinterpret_cast<uint4*>(base + off) = v;
 }
 
-template <class C>
+template <class C, bool kPaged>
 __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const PrefillParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* sQ = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -439,7 +445,16 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         const long long r0 = (long long)kb * C::kBk;
         const int c = tid & 15, rr = tid >> 4;
         PfRaw<C::kKind> raw[kPer];
-        if (r0 + C::kBk <= p.L) {
+        if constexpr (kPaged) {  // through the block table, row by row
+#pragma unroll
+            for (int t = 0; t < kPer; ++t) {
+                const long long gr = min(r0 + rr + kRowStep * t, (long long)p.L - 1);
+                int pg = __ldg(p.block_table + gr / p.page_rows);
+                pg = (pg >= 0 && pg < p.num_pages) ? pg : 0;
+                const long long grow = ((long long)pg * p.Hkv + hk) * p.page_rows + gr % p.page_rows;
+                raw[t] = pf_load<C::kKind, kScale>(codes, scales, grow, c);
+            }
+        } else if (r0 + C::kBk <= p.L) {
             const long long grow = (long long)hk * p.L + r0 + rr;
 #pragma unroll
             for (int t = 0; t < kPer; ++t) raw[t] = pf_load<C::kKind, kScale>(codes, scales, grow + kRowStep * t, c);

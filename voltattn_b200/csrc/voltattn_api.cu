@@ -532,13 +532,18 @@ int launch_prefill(const PrefillParams& p, cudaStream_t st) {
     if (!attr_set[dev]) {
         std::lock_guard<std::mutex> lock(mu);
         if (!attr_set[dev]) {
-            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes));
             attr_set[dev] = true;
         }
     }
     const dim3 grid((unsigned)((p.Lq + C::kBq - 1) / C::kBq), (unsigned)p.Hq);
-    prefill_tc_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
+    if (p.page_rows > 0)
+        prefill_tc_kernel<C, true><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
+    else
+        prefill_tc_kernel<C, false><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }
@@ -1036,7 +1041,8 @@ int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, 
     return decode_impl(fmt, bufs, H, L, D, S, ws, need, nullptr, stream);
 }
 
-int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* stream) {
+static int prefill_impl(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, const int* block_table,
+                        int page_rows, int num_pages, void* stream) {
     if (!is_valid_fmt(fmt) || !b) return VA_ERR_INVALID;
     if (Hq < 1 || Hkv < 1 || Hq % Hkv || Lq < 1 || L < Lq) return VA_ERR_INVALID;
     if (D != 128) return VA_ERR_UNSUPPORTED;
@@ -1057,6 +1063,9 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
     p.Hkv = Hkv;
     p.L = L;
     p.Lq = Lq;
+    p.block_table = block_table;
+    p.page_rows = page_rows;
+    p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (fmt == VA_BF16P) return launch_prefill<PrefillCfg<Kind::BF16>>(p, st);
     if (fmt == VA_Q4CP) return launch_prefill<PrefillCfg<Kind::Q4, true>>(p, st);
@@ -1067,6 +1076,19 @@ int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D,
         case 4: return launch_prefill<PrefillCfg<Kind::Q4>>(p, st);
         default: return launch_prefill<PrefillCfg<Kind::Q3>>(p, st);
     }
+}
+
+int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* stream) {
+    return prefill_impl(fmt, b, Hq, Hkv, L, Lq, D, nullptr, 0, 0, stream);
+}
+
+int va_prefill_paged(int fmt, const va_bufs* b, const int* block_table, int max_pages, int page_rows, int num_pages,
+                     int Hq, int Hkv, int L, int Lq, int D, void* stream) {
+    if (!block_table || page_rows < 1 || num_pages < 1 || max_pages < 1) return VA_ERR_INVALID;
+    if (fmt == VA_Q4CP) return VA_ERR_UNSUPPORTED;  // its V scales are per sequence row, not paged
+    if ((long long)max_pages * page_rows < L) return VA_ERR_INVALID;
+    if ((long long)num_pages * Hkv * page_rows >= (1ll << 40)) return VA_ERR_TOO_LARGE;
+    return prefill_impl(fmt, b, Hq, Hkv, L, Lq, D, block_table, page_rows, num_pages, stream);
 }
 
 int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_host, int H, int L, int D, int S,
