@@ -288,11 +288,13 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         const long long pt0 = tc_tile_row<C>(g, t);
         const int pneed = (int)(min(pt0 + C::kTr, (g.r1 + 7) & ~7ll) - pt0);
         if (lane * C::kBox >= pneed) return 0;
-        const long long yl = pt0 + (long long)lane * C::kBox;
-        const int pg = (int)(yl / p.page_rows);
+        // sequence positions are below 2^31 (checked on the host): 32-bit
+        // division, far cheaper than the emulated 64-bit one
+        const int yl = (int)(pt0 + (long long)lane * C::kBox);
+        const int pg = yl / p.page_rows;
         int pp = pg < p.max_pages ? __ldg(p.block_table + (size_t)g.b * p.max_pages + pg) : 0;
         pp = (pp >= 0 && pp < p.num_pages) ? pp : 0;
-        return (pp * p.Hkv + g.hk) * p.page_rows + (int)(yl % p.page_rows);
+        return (pp * p.Hkv + g.hk) * p.page_rows + (yl - pg * p.page_rows);
     };
     while (ok && u < nunits) {
         int unext = nunits;
