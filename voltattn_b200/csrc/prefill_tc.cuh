@@ -448,10 +448,11 @@ __global__ void __launch_bounds__(C::kThreads, 2) prefill_tc_kernel(const Prefil
         if constexpr (kPaged) {  // through the block table, row by row
 #pragma unroll
             for (int t = 0; t < kPer; ++t) {
-                const long long gr = min(r0 + rr + kRowStep * t, (long long)p.L - 1);
-                int pg = __ldg(p.block_table + gr / p.page_rows);
+                const int gr = (int)min(r0 + rr + kRowStep * t, (long long)p.L - 1);  // L < 2^31: 32-bit division
+                const int pi = gr / p.page_rows;
+                int pg = __ldg(p.block_table + pi);
                 pg = (pg >= 0 && pg < p.num_pages) ? pg : 0;
-                const long long grow = ((long long)pg * p.Hkv + hk) * p.page_rows + gr % p.page_rows;
+                const long long grow = ((long long)pg * p.Hkv + hk) * p.page_rows + (gr - pi * p.page_rows);
                 raw[t] = pf_load<C::kKind, kScale>(codes, scales, grow, c);
             }
         } else if (r0 + C::kBk <= p.L) {
