@@ -283,9 +283,12 @@ __device__ __forceinline__ PfRaw<K> pf_load(const uint8_t* codes, const __half* 
             r.w[1] = v.y;
         } else if constexpr (K == Kind::Q4) {
             r.w[0] = __ldg(reinterpret_cast<const uint32_t*>(src) + c);
-        } else {  // bits 24c .. 24c+23 of the row
-            r.w[0] = (uint32_t)__ldg(src + 3 * c) | ((uint32_t)__ldg(src + 3 * c + 1) << 8) |
-                     ((uint32_t)__ldg(src + 3 * c + 2) << 16);
+        } else {  // bits 24c .. 24c+23 of the row: two aligned words, funnel-shifted
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(src) + ((3 * c) >> 2);
+            const uint32_t sh = 8u * ((3u * c) & 3u);
+            const uint32_t lo = __ldg(w);
+            const uint32_t hi = sh > 8u ? __ldg(w + 1) : 0u;  // word 1 only when the bytes straddle
+            r.w[0] = __funnelshift_r(lo, hi, sh);
         }
     }
     return r;
