@@ -11,8 +11,22 @@ CLI       := voltattn_b200/bin/voltattn
 
 all: $(LIB) $(CLI) oracle
 
-$(LIB): $(CSRC)/voltattn_api.cu $(HDRS)
-	$(NVCC) $(NVFLAGS) -shared -o $@ $(CSRC)/voltattn_api.cu 2> voltattn_b200/ptxas.log || (cat voltattn_b200/ptxas.log; false)
+# One translation unit per kernel family, compiled in parallel as
+# relocatable device code (one device error word shared by all of them) and
+# device-linked into the shared library.
+SRCS      := $(CSRC)/voltattn_api.cu $(CSRC)/host_util.cu $(CSRC)/launch_tc.cu $(CSRC)/launch_tcg.cu \
+             $(CSRC)/launch_mma.cu $(CSRC)/launch_prefill.cu $(CSRC)/launch_stream_g1.cu \
+             $(CSRC)/launch_stream_g2.cu $(CSRC)/launch_stream_g4.cu $(CSRC)/launch_stream_g8.cu
+OBJDIR    := voltattn_b200/_build
+OBJS      := $(patsubst $(CSRC)/%.cu,$(OBJDIR)/%.o,$(SRCS))
+
+$(OBJDIR)/%.o: $(CSRC)/%.cu $(HDRS) $(wildcard $(CSRC)/*.cuh)
+	@mkdir -p $(OBJDIR)
+	$(NVCC) $(NVFLAGS) -rdc=true -c -o $@ $< 2> $@.log || (cat $@.log; false)
+
+$(LIB): $(OBJS)
+	$(NVCC) $(ARCH) -shared -rdc=true -o $@ $(OBJS) -lcuda 2> voltattn_b200/link.log || (cat voltattn_b200/link.log; false)
+	cat $(OBJDIR)/*.o.log > voltattn_b200/ptxas.log
 
 $(CLI): $(CSRC)/cli/voltattn_main.cu $(LIB) $(HDRS)
 	@mkdir -p voltattn_b200/bin
@@ -20,9 +34,9 @@ $(CLI): $(CSRC)/cli/voltattn_main.cu $(LIB) $(HDRS)
 	  -Xlinker -rpath,'$$ORIGIN/..'
 
 oracle:
-	$(MAKE) -C oracle
+	$(MAKE) -C oracle REF_SRC="$(REF_SRC)"
 
 clean:
-	rm -f $(LIB) $(CLI) voltattn_b200/ptxas.log
+	rm -rf $(LIB) $(CLI) voltattn_b200/ptxas.log voltattn_b200/link.log $(OBJDIR)
 
 .PHONY: all oracle clean

@@ -37,10 +37,10 @@ H, D = 32, 128
 FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+": 3, "bf16+": 16, "f8+": 8,
                "q4c+": 4}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the top kernel at
-# L=16384: the ncu captures of profiles/decode_tc_L65536.md (q4+, q8+: tile
-# kernel) and profiles/decode_stream_L65536.md (f16+: streaming kernel), taken
-# at L=65536 (above the L2 size) and scaled by the rows processed (x 1/4);
-# reads equal the algorithmic bytes there. Formats without a capture report None.
+# L=16384, from one ncu capture per kernel taken at L=65536 (above the L2 size)
+# and scaled to L=16384 by the rows processed (x 1/4): traffic grows in
+# proportion to the rows, and the reads equal the algorithmic bytes there.
+# Formats without a capture report None.
 NCU_TRAFFIC_BYTES = {"q4+": int((285.285120e6 + 3.214080e6) / 4),
                      "q8+": int((553.715456e6 + 3.673344e6) / 4),
                      "f16+": int((1073.790e6 + 3.593472e6) / 4)}
@@ -679,7 +679,7 @@ def run_ours(args, rank, world):
         value = world * 1e3 / ms
         traffic = NCU_TRAFFIC_BYTES.get(fmt)
         line = {
-            "metric": f"decode tok/s (batch 1, H={H}, D={D}, L={L}, {fmt}); MBU vs probed read ceiling",
+            "metric": f"decode tok/s (batch 1, H={H}, D={D}, L={L}, {fmt})",
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: fp32 N(0,1) K/V drawn on the GPU from a seed and packed by the GPU quantizer; "

@@ -48,3 +48,31 @@ def test_decode_host_matches_decode(va, oracle, fmt, on_stream):
         want = va.decode(fmt, K, V, sK, sV, qv.cuda(), H, L, D, S).cpu()
         assert torch.equal(got, want), f"{fmt} step {step}: differs from va_decode"
     assert va.device_error() == 0
+
+
+def test_pageable_host_memory_is_rejected_before_any_launch(va):
+    """Ordinary (pageable) host memory cannot be reached by a kernel: the host
+    entry points refuse it with VA_ERR_INVALID instead of launching on it."""
+    import ctypes as C
+
+    import torch
+    lib = va.lib()
+    H, L, D, S = 2, 64, 128, 1
+    K, sK = va.quantize(torch.randn(H * L * D, device="cuda"), 8, H, L, D)
+    q_dev = torch.empty(H * D, dtype=torch.float16, device="cuda")
+    out_dev = torch.empty_like(q_dev)
+    b = va.DeviceBufs(K, K, sK, sK, q_dev, out_dev, va.new_workspace(H, D, S))
+    pageable = np.zeros(H * D + 64, dtype=np.float16)
+    off = (-pageable.ctypes.data) % 16 // 2  # a 16-byte aligned view, so only pinning is wrong
+    host = pageable[off:off + H * D]
+    pinned = torch.empty(H * D, dtype=torch.float16).pin_memory()
+    bb = b.va()
+    ws = b.ws
+    fmt = int(va.Fmt.parse("q8+"))
+    for q_ptr, out_ptr in ((host.ctypes.data, pinned.data_ptr()), (pinned.data_ptr(), host.ctypes.data)):
+        rc = lib.va_decode_host(fmt, C.byref(bb), q_ptr, out_ptr, H, L, D, S, ws.data_ptr(), ws.numel() * ws.element_size(), None)
+        assert rc == 1, rc  # VA_ERR_INVALID
+    assert lib.va_copy_small(q_dev.data_ptr(), host.ctypes.data, H * D * 2, None) == 1
+    assert lib.va_copy_small(host.ctypes.data, q_dev.data_ptr(), H * D * 2, None) == 1
+    torch.cuda.synchronize()
+    assert va.device_error() == 0

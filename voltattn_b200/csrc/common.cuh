@@ -24,8 +24,9 @@ enum DeviceError : int {
 // and returns instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
-// Device error word of this library (one translation unit builds the library).
-__device__ int g_device_error = 0;
+// Device error word of this library, defined once (host_util.cu); the
+// library is built with relocatable device code so every kernel writes it.
+extern __device__ int g_device_error;
 
 __device__ __forceinline__ void report_error(int code) { atomicCAS(&g_device_error, 0, code); }
 

@@ -57,6 +57,18 @@
 
 namespace va {
 
+// Per-CTA event timeline for development builds (-DVA_TC_TIMELINE): eight
+// %globaltimer words per CTA (16 slots), see VA_TL below; the array is defined in
+// launch_tc.cu and read back by va_debug_tc_timeline. Absent in the product.
+#ifdef VA_TC_TIMELINE
+constexpr int kTlCtas = 1024;
+extern __device__ unsigned long long g_tc_timeline[kTlCtas * 16];
+#define VA_TL(slot, v) \
+    do { if (blockIdx.x < kTlCtas) g_tc_timeline[blockIdx.x * 16 + (slot)] = (unsigned long long)(v); } while (0)
+#else
+#define VA_TL(slot, v) do { } while (0)
+#endif
+
 // kChan: K codes with static per-channel scales per head ([H][D], folded into
 // the query once per unit) and V codes with one scale per row ([H][L]);
 // otherwise fp16 scales per 64-element group of every K and V row.
@@ -205,21 +217,26 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 // unit = -1 ends the consumers' loop. Scheduler words (after the per-head
 // tickets): next unit, CTAs finished; the last CTA to finish resets both.
 
+// unit; tile = sequence number of the stage within the unit (0 = first);
+// ntiles = 0 for an empty unit, tile + 1 on the unit's last tile, larger
+// otherwise; trow = the tile's index in its stream (rows a0 + trow * kTr).
 struct TcHeader {
-    int unit, tile, ntiles, pad;
+    int unit, tile, ntiles, trow;
 };
 
 // Unit (head h, split s) of the tile kernel: the head's rows [r0, r1) are cut
-// into tiles of kTr rows starting at the 8-row block of r0 (a0), and split s
-// takes tiles s, s + S, s + 2S, ...: a head's splits sweep its rows side by
+// into T tiles of kTr rows starting at the 8-row block of r0 (a0), and split
+// s takes tiles s, s + S, s + 2S, ...: a head's splits sweep its rows side by
 // side (the online softmax needs no contiguity), which keeps the copies of
 // all CTAs in a narrow window of the cache like one sequential stream.
-// Tile i of the unit starts at tile_row(g, i); rows outside [r0, r1) are masked.
+// Tile i of the stream starts at row a0 + i * kTr; rows outside [r0, r1) are
+// masked.
 struct TcUnit {
     int h, s, S;
     long long r0, r1, a0;
-    int ntiles;
-    int b, hk;  // sequence and KV head (paged cache)
+    int T;       // tiles of the stream
+    int ntiles;  // tiles of this split under the static pattern
+    int b, hk;   // sequence and KV head (paged cache)
 };
 
 // Contiguous streams: rows are the flat rows of [H][L]. Paged cache: rows
@@ -241,21 +258,55 @@ __device__ __forceinline__ TcUnit tc_unit_geom(const DecodeParams& p, int u) {
     }
     g.r1 = g.r0 + len;
     g.a0 = g.r0 & ~7ll;
-    const int T = len > 0 ? (int)((g.r1 - g.a0 + C::kTr - 1) / C::kTr) : 0;
-    g.ntiles = T > g.s ? (T - g.s + p.S - 1) / p.S : 0;
+    g.T = len > 0 ? (int)((g.r1 - g.a0 + C::kTr - 1) / C::kTr) : 0;
+    g.ntiles = g.T > g.s ? (g.T - g.s + p.S - 1) / p.S : 0;
     return g;
 }
 
+// First row of tile i of the unit's stream.
 template <class C>
 __device__ __forceinline__ long long tc_tile_row(const TcUnit& g, int i) {
-    return g.a0 + (long long)(g.s + (long long)i * g.S) * C::kTr;
+    return g.a0 + (long long)i * C::kTr;
 }
+
+#ifdef VA_TC_EARLY_KV
+constexpr bool kTcEarlyKv = true;
+#else
+constexpr bool kTcEarlyKv = false;
+#endif
 
 template <class C>
 __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const CUtensorMap* tmV, uint8_t* stages,
-                            TcHeader* hdr, uint8_t* qring, uint64_t* full, uint64_t* empty) {
+                            TcHeader* hdr, uint8_t* qring, uint64_t* full, uint64_t* empty, uint8_t* qfirst,
+                            uint64_t* qbar) {
     const int lane = threadIdx.x & 31;
     const uint64_t pol = l2_policy_evict_first();
+    // the first unit's query goes to its own buffer ahead of the tiles, so the
+    // consumers prepare it while the tiles are in flight
+    const auto first_query = [&]() {
+        if (lane == 0) {
+            const int h0 = (int)blockIdx.x / p.S;
+            mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
+            if constexpr (C::kChan) {
+                bulk_g2s(qfirst, p.q + (size_t)h0 * C::kD, C::kD * 2, qbar, pol);
+                bulk_g2s(qfirst + C::kD * 2, p.scK + (size_t)h0 * C::kD, C::kD * 2, qbar, pol);
+            } else {
+                bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * C::kD, (uint32_t)C::kQBytes, qbar, pol);
+            }
+        }
+        __syncwarp();
+    };
+    bool waited = !kTcEarlyKv;
+    if (waited) first_query();
+    const auto ensure_wait = [&]() {
+        if (!waited) {
+            grid_dependency_wait();
+            VA_TL(12, global_timer_ns());
+            first_query();
+            waited = true;
+        }
+    };
+    if (lane == 0) VA_TL(11, global_timer_ns());
     const long long nr8 = p.total_rows & ~7ll;
     // q3 rows (48 bytes) are copied as flat byte ranges: a tensor copy issues
     // one request per row, and 48-byte rows straddle 32-byte sectors (about
@@ -284,7 +335,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
     // Paged cache: physical first row of box `lane` of tile t, through the block
     // table (a page index outside the pool reads page 0: no wild access).
     const auto paged_row = [&](const TcUnit& g, int t) -> int {
-        if (p.page_rows <= 0 || g.ntiles <= 0) return 0;
+        if (p.page_rows <= 0 || g.T <= 0) return 0;
         const long long pt0 = tc_tile_row<C>(g, t);
         const int pneed = (int)(min(pt0 + C::kTr, (g.r1 + 7) & ~7ll) - pt0);
         if (lane * C::kBox >= pneed) return 0;
@@ -302,35 +353,53 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         const TcUnit g = tc_unit_geom<C>(p, u);
         const long long r1b = (g.r1 + 7) & ~7ll;
         const long long cend = min(r1b, nr8);
-        const int nt = max(g.ntiles, 1);
-        int py_next = paged_row(g, 0);
-        for (int t = 0; t < nt; ++t, ++k) {
-            if (!asked && t >= nt - 2) {
+        // tile j of the unit: s + j S, -1 past the stream's end
+        const auto static_tile = [&](int j) -> int {
+            const long long v = (long long)g.s + (long long)j * g.S;
+            return v < g.T ? (int)v : -1;
+        };
+        int cur = static_tile(0);
+        int nxt = -1;
+        int py_next = cur >= 0 ? paged_row(g, cur) : 0;
+        if (cur < 0) {  // empty split: the header alone (slot and ticket still count)
+            if (!waited && (k >= C::kStages || !asked)) ensure_wait();
+            if (!asked) {
                 if (lane == 0) unext = (int)gridDim.x + (int)atomicAdd(&sched[0], 1u);
                 asked = true;
             }
-            // paged cache: the next tile's block-table entries are loaded now,
-            // one tile ahead of their use
-            const int py = py_next;
-            py_next = (t + 1 < nt) ? paged_row(g, t + 1) : 0;
             if (!acquire(k)) {
                 ok = false;
                 break;
             }
-            const int stage = k % C::kStages;
-            if (g.ntiles == 0) {  // empty split: the header alone (slot and ticket still count)
-                if (lane == 0) {
-                    hdr[stage] = TcHeader{u, 0, 0, 0};
-                    mbar_arrive(&full[stage]);
-                }
-                __syncwarp();
-                continue;
+            if (lane == 0) {
+                hdr[k % C::kStages] = TcHeader{u, 0, 0, 0};
+                mbar_arrive(&full[k % C::kStages]);
             }
+            __syncwarp();
+            ++k;
+        }
+        for (int t = 0; cur >= 0; ++t, ++k) {
+            if (!waited && (k >= C::kStages || (!asked && t >= g.ntiles - 2))) ensure_wait();
+            if (!asked && t >= g.ntiles - 2) {
+                if (lane == 0) unext = (int)gridDim.x + (int)atomicAdd(&sched[0], 1u);
+                asked = true;
+            }
+            if (!acquire(k)) {
+                ok = false;
+                break;
+            }
+            nxt = static_tile(t + 1);
+            // paged cache: the next tile's block-table entries are loaded now,
+            // one tile ahead of their use
+            const int py = py_next;
+            py_next = nxt >= 0 ? paged_row(g, nxt) : 0;
+            const int stage = k % C::kStages;
+            const int hnt = nxt < 0 ? t + 1 : 0x7FFFFFFF;  // header ntiles: marks the unit's last tile
             uint8_t* sK = stages + (size_t)stage * C::kStageBytes;
             uint8_t* sV = sK + C::kTr * C::kRb;
             uint8_t* sSK = sV + C::kTr * C::kRb;
             uint8_t* sSV = sSK + C::kTr * C::kSbK;
-            const long long t0 = tc_tile_row<C>(g, t);
+            const long long t0 = tc_tile_row<C>(g, cur);
             const long long tend = t0 + C::kTr;
             const int need = (int)(min(tend, r1b) - t0);
             const int nbox = (need + C::kBox - 1) / C::kBox;
@@ -338,8 +407,9 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             const bool paged = p.page_rows > 0;
             const long long rg0 = max(t0, nr8), rg1 = min(tend, g.r1);
             // a unit's first tile also carries the stream's query (and, with
-            // per-channel K scales, the head's channel scales right after it)
-            const uint32_t qb = t == 0 ? (uint32_t)C::kQBytes : 0u;
+            // per-channel K scales, the head's channel scales right after it);
+            // the CTA's first unit has its query in its own buffer
+            const uint32_t qb = t == 0 && u != (int)blockIdx.x ? (uint32_t)C::kQBytes : 0u;
             const auto copy_query = [&]() {
                 if constexpr (C::kChan) {
                     bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kD, C::kD * 2, &full[stage], pol);
@@ -373,7 +443,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
 #pragma unroll
                 for (int b = 0; b < C::kTr / C::kBox; ++b) ys[b] = __shfl_sync(0xffffffffu, py, b);
                 if (lane == 0) {
-                    hdr[stage] = TcHeader{u, t, g.ntiles, 0};
+                    hdr[stage] = TcHeader{u, t, hnt, cur};
                     mbar_arrive_expect_tx(&full[stage],
                                           (uint32_t)nbox * C::kBox * (2u * C::kRb + C::kSbK + C::kSbV) + qb);
                     if (qb) copy_query();
@@ -405,11 +475,8 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                         }
                     }
                 }
-                __syncwarp();
-                continue;
-            }
-            if (lane == 0) {
-                hdr[stage] = TcHeader{u, t, g.ntiles, 0};
+            } else if (lane == 0) {
+                hdr[stage] = TcHeader{u, t, hnt, cur};
                 // flat codes: the tile's rows inside the tensor, one bulk copy
                 // per matrix (rows past the end stay stale; they are masked)
                 const uint32_t crows =
@@ -439,16 +506,27 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 }
             }
             __syncwarp();
+            if (nxt < 0) {
+                ++k;
+                break;
+            }
+            cur = nxt;
         }
         u = __shfl_sync(0xffffffffu, unext, 0);
     }
+    ensure_wait();
     // this CTA's last grab is done: count it; the last CTA resets the schedule
     // (fences: this CTA's grabs are performed before its count, and the reset
     // after every CTA's count)
+    unsigned last = 0;
     if (lane == 0) {
         __threadfence();
-        if (atomicAdd(&sched[1], 1u) == gridDim.x - 1) {
-            __threadfence();
+        last = atomicAdd(&sched[1], 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+        __threadfence();
+        if (lane == 0) {
             sched[0] = 0u;
             sched[1] = 0u;
         }
@@ -918,7 +996,10 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
             return;
         }
         const int h = th[e];
-        if (h < 0) return;
+        if (h < 0) {
+            if (lane == 0) VA_TL(4, global_timer_ns());  // timeline: 4 ticket warp done
+            return;
+        }
         unsigned ticket = 0;
         if (lane == 0) ticket = atomic_add_acq_rel_gpu(&p.counters[h], 1u);
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
@@ -943,6 +1024,7 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
                 }
             }
             if (lane == 0) store_relaxed_gpu(&p.counters[h], 0u);
+            if (lane == 0) VA_TL(5, global_timer_ns());  // timeline: 5 last head merge written
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&tfree[e]);
@@ -990,26 +1072,28 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         fence_mbar_init();
     }
     __syncthreads();
-    grid_dependency_wait();
+    // Programmatic dependent launch: every warp but the producer waits here for
+    // the preceding grid (its ws, counters and out, and the query, which a
+    // preceding kernel may have written). With kTcEarlyKv the producer streams
+    // the first stages of K/V first, which no decode writes, and waits before
+    // it reads the query or touches the schedule counters.
+    if (warp != C::kWarps || !kTcEarlyKv) grid_dependency_wait();
     if (threadIdx.x == 0) grid_launch_dependents();
+    if (threadIdx.x == 0) {  // timeline: 0 start, 1 SM
+        VA_TL(0, global_timer_ns());
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        VA_TL(1, smid);
+    }
 
     const int nunits = p.H * p.S;
     const int h0 = (int)blockIdx.x / p.S;  // head of the CTA's first unit (blockIdx.x < nunits)
     if (warp == C::kWarps) {
         if (lane == 0) {
-            // the first unit's query goes out ahead of the tiles, so the
-            // consumers prepare it while the tiles are in flight
-            mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
-            if constexpr (C::kChan) {
-                bulk_g2s(qfirst, p.q + (size_t)h0 * D, D * 2, qbar, l2_policy_evict_first());
-                bulk_g2s(qfirst + D * 2, p.scK + (size_t)h0 * D, D * 2, qbar, l2_policy_evict_first());
-            } else {
-                bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
-            }
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
-        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty);
+        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar);
         return;
     }
     if (warp == C::kWarps + 1) {
@@ -1072,7 +1156,15 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             break;
         }
         const TcHeader h = hdr[stage];
-        if (h.unit < 0) break;
+        if (tid == 0 && k == 0) VA_TL(2, global_timer_ns());  // timeline: 2 first stage landed
+        if (tid == 0 && k >= 1 && k < 4) VA_TL(7 + k, global_timer_ns());  // 8..10: stages 1..3 landed
+        if (h.unit < 0) {
+            if (tid == 0) {  // timeline: 3 last tile consumed, 6 stages consumed
+                VA_TL(3, global_timer_ns());
+                VA_TL(6, k);
+            }
+            break;
+        }
         uint8_t* base = stages + (size_t)stage * C::kStageBytes;
         if (h.tile == 0) {
             gm = tc_unit_geom<C>(p, h.unit);
@@ -1088,7 +1180,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
                 for (int x = 0; x < (C::kNib ? 4 : 2); ++x) st.o[pi][x] = 0.f;
         }
         if (h.ntiles > 0) {
-            const long long t0 = tc_tile_row<C>(gm, h.tile);
+            const long long t0 = tc_tile_row<C>(gm, h.trow);
             const uint32_t sK = smem_u32(base), sV = sK + C::kTr * C::kRb;
             const __half* sSK = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb);
             const __half* sSV = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb + C::kTr * C::kSbK);
@@ -1151,6 +1243,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         }
     }
     if (tickets && ring_slot_free()) hand_over(-1);
+    if (tid == 0) VA_TL(7, global_timer_ns());  // timeline: 7 consumers done
 }
 
 }  // namespace va

@@ -362,18 +362,17 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         fence_mbar_init();
     }
     __syncthreads();
-    grid_dependency_wait();
+    // programmatic dependent launch: as in decode_tc_kernel
+    if (warp != C::kWarps || !kTcEarlyKv) grid_dependency_wait();
     if (threadIdx.x == 0) grid_launch_dependents();
 
     const int h0 = (int)blockIdx.x / p.S;
     if (warp == C::kWarps) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
-            bulk_g2s(qfirst, p.q + (size_t)h0 * G * D, (uint32_t)C::kQBytes, qbar, l2_policy_evict_first());
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
-        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty);
+        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar);
         return;
     }
     if (warp == C::kWarps + 1) {
@@ -447,7 +446,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
                 for (int x = 0; x < 4; ++x) st.o[ch][x] = 0.f;
         }
         if (h.ntiles > 0) {
-            const long long t0 = tc_tile_row<C>(gm, h.tile);
+            const long long t0 = tc_tile_row<C>(gm, h.trow);
             const uint32_t sK = smem_u32(base), sV = sK + C::kTr * C::kRb;
             const __half* sSK = reinterpret_cast<const __half*>(base + 2 * C::kTr * C::kRb);
             const __half* sSV = sSK + C::kTr * C::kNgrp;

@@ -6,6 +6,7 @@
 #include <climits>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <vector>
 
@@ -20,25 +21,14 @@
 #include "decode_tcg.cuh"
 #include "exchange.cuh"
 #include "prefill_tc.cuh"
+#include "launch.cuh"
 #include "probe.cuh"
 #include "quantize.cuh"
 
 using namespace va;
+using namespace va::host;
 
 namespace {
-
-thread_local int t_last_cuda_error = 0;
-
-int cuda_fail(cudaError_t e) {
-    t_last_cuda_error = (int)e;
-    return VA_ERR_CUDA;
-}
-
-#define VA_CUDA(call)                                   \
-    do {                                                \
-        const cudaError_t e__ = (call);                 \
-        if (e__ != cudaSuccess) return cuda_fail(e__);  \
-    } while (0)
 
 bool is_valid_fmt(int f) { return f >= VA_F16 && f <= VA_Q4CP; }
 bool is_f16(int f) { return f == VA_F16 || f == VA_F16P || f == VA_BF16P; }  // 16-bit rows, no scales
@@ -46,322 +36,9 @@ bool is_plain(int f) { return f == VA_F16 || f == VA_Q8 || f == VA_Q4; }
 int fmt_bits(int f) {
     return is_f16(f) ? 16 : (f == VA_Q8 || f == VA_Q8P || f == VA_F8P) ? 8 : (f == VA_Q3P) ? 3 : 4;  // q4c+: 4
 }
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t slots_bytes(int H, int D, int S) { return (size_t)H * S * (D + 2) * sizeof(float); }
 size_t counters_offset(int H, int D, int S) { return (slots_bytes(H, D, S) + 255) & ~(size_t)255; }
-
-constexpr int kMaxDevices = 64;
-
-int current_device(int* dev) {
-    VA_CUDA(cudaGetDevice(dev));
-    if (*dev < 0 || *dev >= kMaxDevices) return VA_ERR_UNSUPPORTED;
-    return VA_OK;
-}
-
-int sm_count(int dev) {
-    static int cache[kMaxDevices] = {0};
-    if (cache[dev] == 0) {
-        int n = 0;
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev] = n;
-    }
-    return cache[dev];
-}
-
-// Per (kernel configuration, device): dynamic smem attribute set and the
-// number of resident CTAs per SM.
-template <class C>
-int stream_ctas_per_sm(int dev, int* out) {
-    static int occ[kMaxDevices] = {0};
-    static std::mutex mu;
-    if (occ[dev] == 0) {
-        std::lock_guard<std::mutex> lock(mu);
-        if (occ[dev] == 0) {
-            VA_CUDA(cudaFuncSetAttribute(decode_stream_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            int n = 0;
-            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_stream_kernel<C>, C::kThreads,
-                                                                  C::kSmemBytes));
-            occ[dev] = std::max(1, n);
-        }
-    }
-    *out = occ[dev];
-    return VA_OK;
-}
-
-// Which consumer the quantized "+" formats use. Measured on B200: at D = 128
-// the tensor-core tile kernels for batch-1 decode of q4+/q8+ (decode_tc.cuh)
-// and grouped-query decode of q4+ with 4 query heads per KV head
-// (decode_tcg.cuh); for other grouped-query shapes the tensor-core consumer
-// of decode_mma.cuh; otherwise the integer dot-product consumer.
-// VOLTATTN_CONSUMER=dp|mma|tc overrides where the choice applies.
-enum class Consumer { kDp, kMma, kTc };
-
-Consumer pick_consumer(Kind k, int D, int G) {
-    static const int v = [] {
-        const char* e = std::getenv("VOLTATTN_CONSUMER");
-        if (e && std::strcmp(e, "dp") == 0) return 0;
-        if (e && std::strcmp(e, "mma") == 0) return 1;
-        if (e && std::strcmp(e, "tc") == 0) return 2;
-        return -1;
-    }();
-    const bool tc_ok =
-        D == 128 && ((G == 1 && (k == Kind::Q3 || k == Kind::Q4 || k == Kind::Q8)) ||
-                     ((G == 2 || G == 4 || G == 8) && k == Kind::Q4));
-    if (v == 0) return Consumer::kDp;
-    if (v == 1) return Consumer::kMma;
-    if (v == 2 && tc_ok) return Consumer::kTc;
-    if (tc_ok) return Consumer::kTc;
-    return G >= 2 ? Consumer::kMma : Consumer::kDp;
-}
-
-template <class C>
-int mma_ctas_per_sm(int dev, int* out) {
-    static int occ[kMaxDevices] = {0};
-    static std::mutex mu;
-    if (occ[dev] == 0) {
-        std::lock_guard<std::mutex> lock(mu);
-        if (occ[dev] == 0) {
-            VA_CUDA(cudaFuncSetAttribute(decode_mma_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            int n = 0;
-            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<C>, C::kThreads,
-                                                                  C::kSmemBytes));
-            occ[dev] = std::max(1, n);
-        }
-    }
-    *out = occ[dev];
-    return VA_OK;
-}
-
-template <class C>
-int launch_mma(const DecodeParams& p, cudaStream_t st) {
-    int dev, occ;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    rc = mma_ctas_per_sm<C>(dev, &occ);
-    if (rc) return rc;
-    const long long units = (long long)p.H * p.S;
-    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_mma_kernel<C>, p));
-    return VA_OK;
-}
-
-// ---- tensor-core tile kernel: 2-D tensor maps of the K / V codes ---------------------
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            f = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
-// [rows][row_bytes] uint8 codes, boxes of box_rows full rows, swizzle span =
-// row bytes (64 or 128; other widths, the 48-byte q3 rows, unswizzled), zero
-// fill past the last row.
-int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int row_bytes, int box_rows) {
-    const auto enc = tensor_map_encoder();
-    if (!enc) return VA_ERR_UNSUPPORTED;
-    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)row_bytes, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
-                                  : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                    : CU_TENSOR_MAP_SWIZZLE_NONE;
-    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? VA_OK : VA_ERR_UNSUPPORTED;
-}
-
-template <class C>
-int tc_ctas_per_sm(int dev, int* out) {
-    static int occ[kMaxDevices] = {0};
-    static std::mutex mu;
-    if (occ[dev] == 0) {
-        std::lock_guard<std::mutex> lock(mu);
-        if (occ[dev] == 0) {
-            VA_CUDA(cudaFuncSetAttribute(decode_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            int n = 0;
-            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tc_kernel<C>, C::kThreads,
-                                                                  C::kSmemBytes));
-            occ[dev] = std::max(1, n);
-        }
-    }
-    *out = occ[dev];
-    return VA_OK;
-}
-
-template <class C>
-int launch_tc(const DecodeParams& p, cudaStream_t st) {
-    int dev, occ;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    rc = tc_ctas_per_sm<C>(dev, &occ);
-    if (rc) return rc;
-    CUtensorMap tmK, tmV;
-    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, C::kBox);
-    if (rc) return rc;
-    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, C::kBox);
-    if (rc) return rc;
-    const long long units = (long long)p.H * p.S;
-    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tc_kernel<C>, p, tmK, tmV));
-    return VA_OK;
-}
-
-template <class C>
-int tcg_ctas_per_sm(int dev, int* out) {
-    static int occ[kMaxDevices] = {0};
-    static std::mutex mu;
-    if (occ[dev] == 0) {
-        std::lock_guard<std::mutex> lock(mu);
-        if (occ[dev] == 0) {
-            VA_CUDA(cudaFuncSetAttribute(decode_tcg_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            int n = 0;
-            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tcg_kernel<C>, C::kThreads,
-                                                                  C::kSmemBytes));
-            occ[dev] = std::max(1, n);
-        }
-    }
-    *out = occ[dev];
-    return VA_OK;
-}
-
-template <class C>
-int launch_tcg(const DecodeParams& p, cudaStream_t st) {
-    int dev, occ;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    rc = tcg_ctas_per_sm<C>(dev, &occ);
-    if (rc) return rc;
-    CUtensorMap tmK, tmV;
-    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, C::kBox);
-    if (rc) return rc;
-    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, C::kBox);
-    if (rc) return rc;
-    const long long units = (long long)p.H * p.S;
-    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tcg_kernel<C>, p, tmK, tmV));
-    return VA_OK;
-}
-
-template <class C>
-int launch_stream(const DecodeParams& p, cudaStream_t st) {
-    if constexpr (!is_float_kind(C::kKind)) {
-        const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
-        if constexpr (C::kG == 1 && C::kD == 128 &&
-                      (C::kKind == Kind::Q3 || C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
-            // tensor coordinates are 32-bit
-            // and the query is bulk-copied
-            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
-                (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
-                return launch_tc<TcCfg<C::kKind, 128>>(p, st);
-        }
-        if constexpr ((C::kG == 2 || C::kG == 4 || C::kG == 8) && C::kD == 128 && C::kKind == Kind::Q4) {
-            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
-                (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
-                return launch_tcg<TcgCfg<Kind::Q4, 128, C::kG>>(p, st);
-        }
-        if (c == Consumer::kMma) return launch_mma<MmaCfg<C::kKind, C::kD, C::kG>>(p, st);
-    }
-    int dev, occ;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    rc = stream_ctas_per_sm<C>(dev, &occ);
-    if (rc) return rc;
-    const long long units = (long long)p.H * p.S;
-    const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
-    // Programmatic stream serialization: the kernel waits for the preceding
-    // grid before any global access (griddepcontrol.wait), so only its launch
-    // latency and shared-memory prologue overlap the predecessor's tail.
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_stream_kernel<C>, p));
-    return VA_OK;
-}
-
-template <Kind K>
-int launch_stream_d(const DecodeParams& p, int D, cudaStream_t st) {
-    return D == 128 ? launch_stream<StreamCfg<K, 128>>(p, st) : launch_stream<StreamCfg<K, 64>>(p, st);
-}
-
-int launch_stream_fmt(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
-    switch (fmt) {
-        case VA_BF16P: return launch_stream_d<Kind::BF16>(p, D, st);
-        case VA_F8P: return launch_stream_d<Kind::F8>(p, D, st);
-        case VA_F16P: return launch_stream_d<Kind::F16>(p, D, st);
-        case VA_Q8P: return launch_stream_d<Kind::Q8>(p, D, st);
-        case VA_Q4P: return launch_stream_d<Kind::Q4>(p, D, st);
-        case VA_Q3P: return launch_stream_d<Kind::Q3>(p, D, st);
-        default: return VA_ERR_INVALID;
-    }
-}
-
-template <Kind K, int G>
-int launch_stream_dg(const DecodeParams& p, int D, cudaStream_t st) {
-    return D == 128 ? launch_stream<StreamCfg<K, 128, G>>(p, st) : launch_stream<StreamCfg<K, 64, G>>(p, st);
-}
-
-template <int G>
-int launch_stream_fmt_g(int fmt, const DecodeParams& p, int D, cudaStream_t st) {
-    switch (fmt) {
-        case VA_BF16P: return launch_stream_dg<Kind::BF16, G>(p, D, st);
-        case VA_F8P: return launch_stream_dg<Kind::F8, G>(p, D, st);
-        case VA_F16P: return launch_stream_dg<Kind::F16, G>(p, D, st);
-        case VA_Q8P: return launch_stream_dg<Kind::Q8, G>(p, D, st);
-        case VA_Q4P: return launch_stream_dg<Kind::Q4, G>(p, D, st);
-        case VA_Q3P: return launch_stream_dg<Kind::Q3, G>(p, D, st);
-        default: return VA_ERR_UNSUPPORTED;
-    }
-}
 
 size_t gqa_ws_bytes(int B, int Hq, int Hkv, int D, int S) {
     const size_t slots = (size_t)B * Hq * S * (D + 2) * sizeof(float);
@@ -425,40 +102,6 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     return p;
 }
 
-int stream_cfg_tile_rows(int fmt, int D) {
-    switch (fmt) {
-        case VA_BF16P: return D == 128 ? StreamCfg<Kind::BF16, 128>::kTr : StreamCfg<Kind::BF16, 64>::kTr;
-        case VA_F8P: return D == 128 ? StreamCfg<Kind::F8, 128>::kTr : StreamCfg<Kind::F8, 64>::kTr;
-        case VA_F16P: return D == 128 ? StreamCfg<Kind::F16, 128>::kTr : StreamCfg<Kind::F16, 64>::kTr;
-        case VA_Q8P: return D == 128 ? StreamCfg<Kind::Q8, 128>::kTr : StreamCfg<Kind::Q8, 64>::kTr;
-        case VA_Q4P: return D == 128 ? StreamCfg<Kind::Q4, 128>::kTr : StreamCfg<Kind::Q4, 64>::kTr;
-        default: return D == 128 ? StreamCfg<Kind::Q3, 128>::kTr : StreamCfg<Kind::Q3, 64>::kTr;
-    }
-}
-
-int stream_cfg_occupancy(int fmt, int D, int dev, int* occ) {
-    switch (fmt) {
-        case VA_BF16P:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::BF16, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::BF16, 64>>(dev, occ);
-        case VA_F8P:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::F8, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::F8, 64>>(dev, occ);
-        case VA_F16P:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::F16, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::F16, 64>>(dev, occ);
-        case VA_Q8P:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q8, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::Q8, 64>>(dev, occ);
-        case VA_Q4P:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q4, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::Q4, 64>>(dev, occ);
-        default:
-            return D == 128 ? stream_ctas_per_sm<StreamCfg<Kind::Q3, 128>>(dev, occ)
-                            : stream_ctas_per_sm<StreamCfg<Kind::Q3, 64>>(dev, occ);
-    }
-}
-
 int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws, size_t ws_bytes, float* partial,
                 void* stream) {
     int rc = check_decode_args(fmt, b, H, L, D, S);
@@ -488,7 +131,7 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
             VA_CUDA(cudaGetLastError());
         } else {
             const DecodeParams p = make_params(b, H, L, S, slots, nullptr, kOutSlots, nullptr);
-            rc = launch_stream_fmt(fmt, p, D, st);
+            rc = launch_stream_fmt_g<1>(fmt, p, D, st);
             if (rc) return rc;
         }
         combine_kernel<<<H, kCombineThreads, 0, st>>>(slots, 1, H, S, D, static_cast<__half*>(b->out), nullptr, 0);
@@ -498,7 +141,7 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
     unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
     const DecodeParams p =
         make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
-    return launch_stream_fmt(fmt, p, D, st);
+    return launch_stream_fmt_g<1>(fmt, p, D, st);
 }
 
 // Fixed workspace of va_decode_noalloc (see include/voltattn.h). In host
@@ -522,32 +165,6 @@ int noalloc_scratch(int dev, void** out) {
 
 }  // namespace
 
-template <class C>
-int launch_prefill(const PrefillParams& p, cudaStream_t st) {
-    int dev;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    static bool attr_set[kMaxDevices] = {false};
-    static std::mutex mu;
-    if (!attr_set[dev]) {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!attr_set[dev]) {
-            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            VA_CUDA(cudaFuncSetAttribute(prefill_tc_kernel<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
-            attr_set[dev] = true;
-        }
-    }
-    const dim3 grid((unsigned)((p.Lq + C::kBq - 1) / C::kBq), (unsigned)p.Hq);
-    if (p.page_rows > 0)
-        prefill_tc_kernel<C, true><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
-    else
-        prefill_tc_kernel<C, false><<<grid, C::kThreads, C::kSmemBytes, st>>>(p);
-    VA_CUDA(cudaGetLastError());
-    return VA_OK;
-}
-
 // ---- decode with host-side q / out: one cached CUDA graph per argument set ----
 struct HostStepKey {
     int dev, fmt, H, L, D, S;
@@ -559,9 +176,12 @@ struct HostStepKey {
     cudaStream_t st;
     bool operator==(const HostStepKey& o) const { return std::memcmp(this, &o, sizeof(*this)) == 0; }
 };
+// The cached executable graph is shared: a launch holds a reference until it
+// has synchronised, so evicting the entry meanwhile cannot destroy it.
+using GraphExecRef = std::shared_ptr<CUgraphExec_st>;
 struct HostStepGraph {
     HostStepKey key;
-    cudaGraphExec_t exec;
+    GraphExecRef exec;
 };
 constexpr size_t kHostStepGraphs = 16;  // cached graphs (oldest evicted)
 std::mutex g_host_step_mu;
@@ -605,7 +225,7 @@ const char* va_status_string(int status) {
     }
 }
 
-int va_last_cuda_error(void) { return t_last_cuda_error; }
+int va_last_cuda_error(void) { return last_cuda_error(); }
 
 size_t va_workspace_bytes(int H, int D, int S) {
     if (H < 1 || S < 1 || D < 1) return 0;
@@ -747,14 +367,42 @@ __global__ void __launch_bounds__(256) copy_small_kernel(uint4* __restrict__ dst
 }
 }  // namespace
 
+namespace {
+// The address a kernel uses for p: device (or managed) memory as is, pinned
+// host memory through its device mapping. Ordinary pageable host memory, which
+// a kernel cannot reach, and unknown pointers give VA_ERR_INVALID, so no kernel
+// is ever launched on them.
+int device_view(const void* p, void** out) {
+    cudaPointerAttributes a;
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();  // the failed query leaves no error behind
+        return VA_ERR_INVALID;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+        *out = const_cast<void*>(p);
+        return VA_OK;
+    }
+    if (a.type == cudaMemoryTypeHost && a.devicePointer) {
+        *out = a.devicePointer;
+        return VA_OK;
+    }
+    return VA_ERR_INVALID;
+}
+}  // namespace
+
 int va_copy_small(void* dst, const void* src, size_t bytes, void* stream) {
     if (!dst || !src) return VA_ERR_INVALID;
     if (!aligned16(dst) || !aligned16(src) || (bytes & 15u)) return VA_ERR_ALIGN;
     if (bytes == 0) return VA_OK;
+    void *d = nullptr, *s = nullptr;
+    int rc = device_view(dst, &d);
+    if (!rc) rc = device_view(src, &s);
+    if (rc) return rc;
     const size_t n16 = bytes / 16;
     const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 1184);
-    copy_small_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint4*>(dst),
-                                                                            static_cast<const uint4*>(src), n16);
+    copy_small_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint4*>(d),
+                                                                            static_cast<const uint4*>(s), n16);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }
@@ -1034,7 +682,11 @@ int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, 
     r = noalloc_scratch(dev, &ws);
     if (r) return r;
     // the array keeps the previous call's contents: zero the counters the
-    // fused combine expects, in stream order before the decode
+    // fused combine expects, in stream order before the decode. This stays
+    // unconditional: a previous call with another geometry left slot floats
+    // where these counters sit, and one whose kernel stopped early (a bounded
+    // wait that gave up) left counters set, which the host cannot see without
+    // a synchronising read. The cost is one small memset per call.
     unsigned char* base = static_cast<unsigned char*>(ws);
     VA_CUDA(cudaMemsetAsync(base + counters_offset(H, D, S), 0, need - counters_offset(H, D, S),
                             static_cast<cudaStream_t>(stream)));
@@ -1067,15 +719,7 @@ static int prefill_impl(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int L
     p.page_rows = page_rows;
     p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (fmt == VA_BF16P) return launch_prefill<PrefillCfg<Kind::BF16>>(p, st);
-    if (fmt == VA_Q4CP) return launch_prefill<PrefillCfg<Kind::Q4, true>>(p, st);
-    if (fmt == VA_F8P) return launch_prefill<PrefillCfg<Kind::F8>>(p, st);
-    switch (fmt_bits(fmt)) {
-        case 16: return launch_prefill<PrefillCfg<Kind::F16>>(p, st);
-        case 8: return launch_prefill<PrefillCfg<Kind::Q8>>(p, st);
-        case 4: return launch_prefill<PrefillCfg<Kind::Q4>>(p, st);
-        default: return launch_prefill<PrefillCfg<Kind::Q3>>(p, st);
-    }
+    return launch_prefill_fmt(fmt, p, st);
 }
 
 int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* stream) {
@@ -1099,14 +743,20 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
     // memory takes plain global stores; the synchronize below makes them
     // visible to the host); the query is copied in first, since the tile
     // kernels bulk-copy it
+    // pageable host memory is rejected here, before any launch: a kernel
+    // cannot reach it (cached graphs below were built from validated pointers)
+    void *q_dev = nullptr, *out_dev = nullptr;
+    int rc = device_view(q_host, &q_dev);
+    if (!rc) rc = device_view(out_host, &out_dev);
+    if (rc) return rc;
     va_bufs b2 = *bufs;
-    b2.out = out_host;
-    int rc = check_decode_args(fmt, &b2, H, L, D, S);
+    b2.out = out_dev;
+    rc = check_decode_args(fmt, &b2, H, L, D, S);
     if (rc) return rc;
     const size_t bytes = (size_t)H * D * sizeof(__half);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const auto step = [&]() -> int {
-        int r = va_copy_small(const_cast<void*>(bufs->q), q_host, bytes, st);
+        int r = va_copy_small(const_cast<void*>(bufs->q), q_dev, bytes, st);
         if (!r) r = decode_impl(fmt, &b2, H, L, D, S, ws, ws_bytes, nullptr, st);
         return r;
     };
@@ -1131,17 +781,18 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
     key.ws = ws;
     key.ws_bytes = ws_bytes;
     key.st = st;
-    cudaGraphExec_t exec = nullptr;
+    GraphExecRef cached;
     {
         std::lock_guard<std::mutex> lock(g_host_step_mu);
         for (const auto& g : g_host_steps)
-            if (g.key == key) exec = g.exec;
+            if (g.key == key) cached = g.exec;
     }
-    if (exec) {
-        VA_CUDA(cudaGraphLaunch(exec, st));
+    if (cached) {
+        VA_CUDA(cudaGraphLaunch(cached.get(), st));
         VA_CUDA(cudaStreamSynchronize(st));
         return VA_OK;
     }
+    cudaGraphExec_t exec = nullptr;
     // first call with these arguments: run directly (also the warm-up of the
     // decode's one-time set-up), then capture the same three launches
     rc = step();
@@ -1158,12 +809,10 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
     const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (ei != cudaSuccess) return VA_ERR_CUDA;
+    GraphExecRef ref(exec, [](cudaGraphExec_t x) { cudaGraphExecDestroy(x); });
     std::lock_guard<std::mutex> lock(g_host_step_mu);
-    if (g_host_steps.size() >= kHostStepGraphs) {
-        cudaGraphExecDestroy(g_host_steps.front().exec);
-        g_host_steps.erase(g_host_steps.begin());
-    }
-    g_host_steps.push_back(HostStepGraph{key, exec});
+    if (g_host_steps.size() >= kHostStepGraphs) g_host_steps.erase(g_host_steps.begin());
+    g_host_steps.push_back(HostStepGraph{key, std::move(ref)});
     return VA_OK;
 }
 
