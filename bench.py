@@ -70,6 +70,7 @@ def parse_args():
                     help="formats also timed for the per-format table (empty: none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the GQA / split-L extra measurements")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the context-length sweep (config 4)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
     ap.add_argument("--prefill-lq", type=int, default=0,
@@ -205,6 +206,56 @@ def cpu_baseline_leg(L, fmt):
                       f"reference's dq), heads over {threads} threads, double-precision reference()"}
 
 
+REF_FMT_INDEX = {"f16": 0, "f16+": 1, "q8": 2, "q8+": 3, "q4": 4, "q4+": 5, "q3+": 6}
+
+
+def reference_kernels_leg(L=16384, n=200):
+    """The reference's own kernels rebuilt for sm_100a (oracle/_ref, its
+    unmodified translation unit) on this GPU: n back-to-back launch() calls
+    per format (its decode kernel plus its combine, legacy default stream,
+    CUDA events around the loop), the reference bench's split rule
+    (src/voltattn.cu:1026), caches quantized by the reference's own host
+    quantize() and rotated over > 4x L2. The GPU speed bar for our kernels."""
+    import torch
+    from oracle.oracle import RefLib
+    lib = RefLib()
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(99)
+    n_el = H * L * D
+    kx = rng.standard_normal(n_el, dtype=np.float32)
+    vx = rng.standard_normal(n_el, dtype=np.float32)
+    q = torch.from_numpy(lib.f2h(rng.standard_normal(H * D, dtype=np.float32)).view(np.int16)).to(dev)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    S = max(1, min(nsm * 2 // H, (L + 511) // 512))
+    out = torch.empty(H * D, dtype=torch.int16, device=dev)
+    ws = torch.empty(H * S * (D + 2), dtype=torch.float32, device=dev)
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
+    res = {}
+    packed = {}
+    for f, idx in REF_FMT_INDEX.items():
+        bits = FORMAT_BITS[f]
+        if bits == 16:
+            tensors = [torch.from_numpy(lib.f2h(x).view(np.int16)).to(dev) for x in (kx, vx)] + [None, None]
+        else:
+            if bits not in packed:
+                kc, ks = lib.quantize(kx, H, L, D, bits)
+                vc, vs = lib.quantize(vx, H, L, D, bits)
+                packed[bits] = [torch.from_numpy(a.view(np.uint8)).to(dev) for a in (kc, vc, ks, vs)]
+            tensors = packed[bits]
+        nbytes = algorithmic_bytes(f, L)
+        copies = max(2, math.ceil(4 * l2 / nbytes))
+        caches = [tensors] + [[None if t is None else t.clone() for t in tensors] for _ in range(copies - 1)]
+        ptrs = [tuple(None if t is None else t.data_ptr() for t in c) for c in caches]
+        torch.cuda.synchronize(dev)
+        ms = lib.time_launches(idx, ptrs, q.data_ptr(), out.data_ptr(), ws.data_ptr(), H, L, D, S, n)
+        res[f] = {"ms": ms, "gbs": nbytes / (ms * 1e6), "tok_s": 1e3 / ms, "splits": S}
+        del caches
+        torch.cuda.empty_cache()
+    return {"workload": f"the reference's launch() rebuilt for sm_100a, batch-1 decode H={H} D={D} L={L}",
+            "timing": f"{n} back-to-back launches per format, CUDA events, caches rotated over > 4x L2",
+            "formats": res}
+
+
 def run_reference_arm(args, rank):
     if rank != 0:
         return
@@ -233,17 +284,30 @@ def run_reference_arm(args, rank):
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads if positions is None else 1,
                              "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if kind == "reference" and not args.no_extra:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                line["extra"] = {"reference_kernels_sm100a": reference_kernels_leg(L)}
+        except Exception as e:  # the CPU line stands without the GPU speed bar
+            line["extra"] = {"reference_kernels_sm100a": {"unavailable": f"{type(e).__name__}: {e}"}}
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------ GPU path --------
 
-def make_cache(va, torch, fmt, L, seed, dev):
+def make_cache(va, torch, fmt, L, seed, dev, outliers=False):
+    """Synthetic cache of one sequence: fp32 N(0,1) K/V from a seeded GPU
+    generator, packed into fmt by the GPU quantizers. outliers: 1 % of the K
+    entries (a seeded mask) scaled x8, which stresses the group scales
+    (BASELINE config 4)."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     n = H * L * D
     kx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
     vx = torch.randn(n, generator=g, device=dev, dtype=torch.float32)
+    if outliers:
+        kx[torch.rand(n, generator=g, device=dev) < 0.01] *= 8.0
     bits = FORMAT_BITS[fmt]
     if fmt == "bf16+":
         K, V, sK, sV = kx.bfloat16(), vx.bfloat16(), None, None
@@ -262,12 +326,12 @@ def make_cache(va, torch, fmt, L, seed, dev):
     return K, V, sK, sV
 
 
-def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, splits=None):
+def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, splits=None, outliers=False):
     """Returns (ms_per_step, S, copies, launches_per_step) for K_steps decodes."""
     nbytes = algorithmic_bytes(fmt, L)
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
     copies = max(2, math.ceil(4 * l2 / nbytes))
-    base = make_cache(va, torch, fmt, L, seed, dev)
+    base = make_cache(va, torch, fmt, L, seed, dev, outliers)
     caches = [base] + [tuple(None if t is None else t.clone() for t in base) for _ in range(copies - 1)]
     q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 1)).half()
     out = torch.empty(H * D, dtype=torch.float16, device=dev)
@@ -279,6 +343,9 @@ def time_format(va, torch, fmt, L, K_steps, W, dev, dist, seed, soak_s=0.3, spli
     def step(i):
         va.launch(fmt, bufs[i % copies], H, L, D, S, stream)
 
+    # the caches and the zeroed workspace come from the default stream: make
+    # them complete before the decode stream reads them
+    torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
         for i in range(max(3, W)):
             step(i)
@@ -350,6 +417,7 @@ def e2e_leg(va, torch, fmt, L, K_steps, dev, dist, seed):
     out = torch.empty(H * D, dtype=torch.float16, device=dev)
     stream = torch.cuda.Stream(device=dev)
     bufs = [va.DeviceBufs(*c, q, out, ws) for c in caches]
+    torch.cuda.synchronize(dev)  # inputs made on the default stream are complete
 
     # host side through numpy views of the pinned buffers (cheaper than torch ops)
     q_src_np, q_pin_np = q_src.numpy(), q_pin.numpy()
@@ -448,6 +516,7 @@ def paged_leg(va, torch, dev, steps, page_rows=256, seed=4242, fmt="q4+", B=64, 
     pb = va.DeviceBufs(pK, pV, psK, psV, b.q, b.out, b.ws)
     b.K = b.V = b.scK = b.scV = None  # the contiguous cache is no longer needed
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)  # inputs made on the default stream are complete
 
     def run():
         va.decode_paged(fmt, pb, table, max_pages, lens_d, B, Hq, Hkv, page_rows, num_pages, D, S, stream)
@@ -484,6 +553,7 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
     kernel (S = 1, 2, 4, 8, 16: 0.354, 0.280, 0.247, 0.256, 0.291 ms)."""
     b, lens_d, nbytes = make_gqa(va, torch, dev, seed, fmt, B, Hq, Hkv, Lmax, S)
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)  # inputs made on the default stream are complete
     with torch.cuda.stream(stream):
         for _ in range(3):
             va.decode_gqa(fmt, b, lens_d, B, Hq, Hkv, Lmax, D, S, stream)
@@ -540,6 +610,7 @@ def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=1
     peak (the kernel computes fp16 x fp16 -> fp32)."""
     b = make_prefill(va, torch, dev, fmt, Hq, Hkv, L, Lq, 5150)
     stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)  # inputs made on the default stream are complete
     with torch.cuda.stream(stream):
         for _ in range(3):
             va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream)
@@ -564,6 +635,52 @@ def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=1
             "reps": reps, "device_error": err}
 
 
+SWEEP_FORMATS = ("f16", "f16+", "q8", "q8+", "q4", "q4+", "q3+")
+SWEEP_L = (1024, 4096, 16384, 65536)
+
+
+def sweep_leg(va, torch, dev, probe, steps=300):
+    """batch-1 decode, H=32, D=128, every reference format
+    at L in {1024, 4096, 16384, 65536}, N(0,1) q/K/V with 1 % of the K entries
+    scaled x8; MBU against the live read probe per (format, L). Each point is
+    a CUDA graph of back-to-back decodes over rotating copies (> 4x L2)."""
+    out = {}
+    for L in SWEEP_L:
+        row = {}
+        for f in SWEEP_FORMATS:
+            ms, S, _, _ = time_format(va, torch, f, L, steps, 3, dev, None, 4000 + L, soak_s=0.0, outliers=True)
+            gbs = algorithmic_bytes(f, L) / (ms * 1e6)
+            row[f] = {"us": round(ms * 1e3, 3), "gbs": round(gbs, 1), "mbu_probe": round(gbs / probe, 4),
+                      "tok_s": round(1e3 / ms, 1), "splits": S}
+            torch.cuda.empty_cache()
+        out[str(L)] = row
+    return {"workload": f"batch-1 decode H={H} D={D}, 1% of K x8, formats {','.join(SWEEP_FORMATS)}",
+            "probe_gbs": probe, "points": out}
+
+
+def accuracy_leg(va, torch, dev, L=4096, seed=31):
+    """H=32, D=128, L=4096, q/K/V N(0,1); the quantized
+    decodes against the fp16 attention output (f16+ over the fp16-rounded
+    cache), i.e. the quantization error the reference's selftest keeps out of
+    its gate. Max and mean |difference| over the H*D outputs."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n = H * L * D
+    kx = torch.randn(n, generator=g, device=dev)
+    vx = torch.randn(n, generator=g, device=dev)
+    q = torch.randn(H * D, generator=g, device=dev).half()
+    ref = va.decode("f16+", kx.half(), vx.half(), None, None, q, H, L, D, va.suggest_splits("f16+", H, L, D)).float()
+    res = {"workload": f"H={H} D={D} L={L}, N(0,1) q/K/V, vs the fp16 (f16+) attention output",
+           "ref_abs_mean": float(ref.abs().mean())}
+    for f in ("q8+", "q4+", "q3+"):
+        bits = FORMAT_BITS[f]
+        K, sK = va.quantize(kx, bits, H, L, D)
+        V, sV = va.quantize(vx, bits, H, L, D)
+        got = va.decode(f, K, V, sK, sV, q, H, L, D, va.suggest_splits(f, H, L, D)).float()
+        err = (got - ref).abs()
+        res[f] = {"max_abs": float(err.max()), "mean_abs": float(err.mean())}
+    return res
+
+
 def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
     """BASELINE config 3 across GPUs: one sequence of L positions split into
     contiguous ranges per rank; each rank decodes its range into per-head
@@ -573,7 +690,17 @@ def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
     from voltattn_b200.launcher import SplitL, SplitLPeer
     sl = SplitLPeer(L, H, D, dev)
     Lr = sl.local_len
-    K, V, sK, sV = make_cache(va, torch, fmt, Lr, 777 + sl.rank, dev)
+    # one seeded cache of the whole sequence (the same on every rank); rank r
+    # keeps its contiguous range [j0, j1) of every head's rows
+    full = make_cache(va, torch, fmt, L, 777, dev)
+    rb = D * FORMAT_BITS[fmt] // 8
+
+    def rows(t, width):
+        return None if t is None else t.view(H, L, width)[:, sl.j0:sl.j1].contiguous().view(-1)
+
+    K, V = rows(full[0], rb), rows(full[1], rb)
+    sK = rows(full[2].view(torch.uint8), 2 * (D // 64)).view(torch.float16)
+    sV = rows(full[3].view(torch.uint8), 2 * (D // 64)).view(torch.float16)
     q = torch.randn(H * D, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).half()
     S = S or va.suggest_splits(fmt, H, Lr, D)
     ws = va.new_workspace(H, D, S, dev)
@@ -603,12 +730,46 @@ def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item()), n
 
+    # parity: both exchanges against one GPU's decode of the whole cache
+    q_full = q
+    out_full = va.decode(fmt, *full, q_full, H, L, D, va.suggest_splits(fmt, H, L, D)).float()
+    del full
+    out_fused = torch.empty(H * D, dtype=torch.float16, device=dev)
+    bf = va.DeviceBufs(K, V, sK, sV, q, out_fused, ws)
+    got_nccl = SplitL.decode(sl, pfn).float()
+    got_p2p = sl.decode_peer(pfn, out).float().clone()
+    got_fused = sl.decode_fused(fmt, bf, S).float().clone()
+    torch.cuda.synchronize(dev)
+
+    def check(got):
+        err = (got - out_full).abs()
+        ok = bool((err <= 2e-3 + 1e-3 * out_full.abs()).all())
+        t = torch.tensor([float(err.max()), 0.0 if ok else 1.0], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0]), t[1].item() == 0.0
+
+    err_nccl, ok_nccl = check(got_nccl)
+    err_p2p, ok_p2p = check(got_p2p)
+    err_fused, ok_fused = check(got_fused)
     ms_nccl, n = timed(lambda: SplitL.decode(sl, pfn))
     ms_p2p, _ = timed(lambda: sl.decode_peer(pfn, out))
+    ms_fused, _ = timed(lambda: sl.decode_fused(fmt, bf, S))
     return {"workload": f"split-L decode, one sequence, H={H} D={D} L={L} {fmt} over {world} GPUs",
-            "ms": ms_p2p, "tok_s": 1e3 / ms_p2p, "gbs": algorithmic_bytes(fmt, L) / (ms_p2p * 1e6),
-            "exchange": "fused peer-memory exchange + combine kernel over NVLink (2 launches per step)",
-            "ms_nccl_allgather": ms_nccl, "steps": n, "scaling": "strong", "launches_per_step": 2}
+            "ms": ms_fused, "tok_s": 1e3 / ms_fused, "gbs": algorithmic_bytes(fmt, L) / (ms_fused * 1e6),
+            "exchange": "peer-memory exchange and merge fused into the decode (va_decode_splitl, 1 launch per step)",
+            "ms_peer_2launch": ms_p2p, "ms_nccl_allgather": ms_nccl, "steps": n, "scaling": "strong",
+            "launches_per_step": 1, "local_rows_per_head": Lr, "splits": S,
+            "parity": {"against": "1-GPU decode of the same seeded full cache", "tol": "2e-3 + 1e-3*|ref|",
+                       "max_err_fused": err_fused, "ok_fused": ok_fused, "max_err_peer": err_p2p, "ok_peer": ok_p2p,
+                       "max_err_nccl": err_nccl, "ok_nccl": ok_nccl}}
+
+
+def splitl_base_leg(va, torch, dev, steps, fmt, L=131072):
+    """The N=1 base of config 3: the whole sequence on one GPU (strong-scaling
+    reference point for splitl_config3 at N > 1)."""
+    ms, S, copies, _ = time_format(va, torch, fmt, L, max(50, min(steps, 500)), 3, dev, None, 777, soak_s=0.0)
+    return {"workload": f"decode, one sequence, H={H} D={D} L={L} {fmt} on 1 GPU", "ms": ms, "tok_s": 1e3 / ms,
+            "gbs": algorithmic_bytes(fmt, L) / (ms * 1e6), "splits": S, "copies": copies}
 
 
 def run_ours(args, rank, world):
@@ -669,9 +830,18 @@ def run_ours(args, rank, world):
             for pf in ("q4+", "f16+"):
                 extra[f"prefill_{pf}"] = prefill_leg(va, torch, dev, pf)
                 torch.cuda.empty_cache()
-        else:
-            extra["splitl_config3"] = splitl_leg(va, torch, dev, dist, world, K)
+            for sf in ("q4+", "q3+"):
+                extra[f"splitl_config3_base_{sf}"] = splitl_base_leg(va, torch, dev, K, sf)
+                torch.cuda.empty_cache()
+            extra["accuracy_config1"] = accuracy_leg(va, torch, dev)
             torch.cuda.empty_cache()
+            if not args.no_sweep:
+                extra["sweep_config4"] = sweep_leg(va, torch, dev, probe)
+                torch.cuda.empty_cache()
+        else:
+            for sf in ("q4+", "q3+"):
+                extra[f"splitl_config3_{sf}"] = splitl_leg(va, torch, dev, dist, world, K, fmt=sf)
+                torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_leg(L, fmt)

@@ -160,6 +160,29 @@ VA_API size_t va_exchange_buffer_bytes(int R, int H, int D);
 VA_API int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
                                unsigned epoch, void* out, void* stream);
 
+/* Split-L across GPUs in one launch per step (launch, src/voltattn.cu:803-835,
+ * plus combine, :651-672, lifted across R GPUs): this rank decodes its range
+ * [j0, j1) of every head's positions (K/V/scales of L = j1 - j0 rows per head,
+ * layout as va_decode; S splits; fused workspace ws_bytes >=
+ * va_workspace_bytes(H, D, S)), and the CTA that completes head h exchanges
+ * the head's partial with the other ranks through peer_buffers (as
+ * va_exchange_combine: va_exchange_buffer_bytes(R, H, D) each, mapped into
+ * this process, zeroed once; epoch = 1, 2, 3, ... the same on all ranks) and
+ * writes the merged fp16 output [H][D] on every rank. q3+/q4+/q8+ at D = 128
+ * on the tile kernel; other formats return VA_ERR_UNSUPPORTED (use
+ * va_decode_partial + va_exchange_combine). Waits are bounded (~1 s, then
+ * va_device_error = peer wait). */
+/* Wall-clock limit of the split-L waits for the peers' partials
+ * (va_exchange_combine, va_decode_splitl) in later launches: default 1 s,
+ * 0 < seconds <= 60. A wait that runs out leaves the head's output untouched
+ * and sets va_device_error to the peer-wait code (4). No reference
+ * counterpart (the reference is single-GPU and exits on CUDA errors,
+ * src/voltattn.cu:49-58). */
+VA_API int va_set_peer_wait_limit(double seconds);
+
+VA_API int va_decode_splitl(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes,
+                            int R, int rank, void* const* peer_buffers, unsigned epoch, void* stream);
+
 /* Log-sum-exp merge (combine, src/voltattn.cu:651-672) of R*S slots per head:
  * slots = float [R][H][S][D+2] (R = 1 is the reference's workspace layout; R > 1
  * is R gathered va_decode_partial / workspace blocks, e.g. one per GPU).

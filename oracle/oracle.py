@@ -249,6 +249,9 @@ class RefLib:
         lib.ref_fill_fast.argtypes = [_f32p, C.c_size_t, C.c_uint64]
         lib.ref_launch.argtypes = [C.c_int] + [C.c_void_p] * 7 + [C.c_int] * 5
         lib.ref_launch.restype = C.c_int
+        lib.ref_time_launches.argtypes = [C.c_int] + [C.c_void_p] * 4 + [C.c_int] + [C.c_void_p] * 3 + \
+            [C.c_int] * 5 + [C.POINTER(C.c_float)]
+        lib.ref_time_launches.restype = C.c_int
         lib.ref_probe_ceiling.restype = C.c_double
         lib.ref_selftest.restype = C.c_int
 
@@ -274,6 +277,20 @@ class RefLib:
         else:
             self.lib.ref_reference(*args)
         return out
+
+    def time_launches(self, fmt: int, caches, q_ptr, out_ptr, ws_ptr, H, L, D, S, n):
+        """Average ms of n back-to-back reference launch() calls (GPU box only),
+        rotating over caches = [(K, V, scK, scV) device pointers]."""
+        k = len(caches)
+        arr = lambda i: (C.c_void_p * k)(*[c[i] for c in caches])  # noqa: E731
+        has_scales = caches[0][2] is not None
+        ms = C.c_float(0.0)
+        rc = self.lib.ref_time_launches(fmt, arr(0), arr(1), arr(2) if has_scales else None,
+                                        arr(3) if has_scales else None, k, q_ptr, out_ptr, ws_ptr, H, L, D, S, n,
+                                        C.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"ref_time_launches failed ({rc})")
+        return ms.value
 
     def fill_fast(self, n, seed):
         v = np.empty(n, np.float32)

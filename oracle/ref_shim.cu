@@ -133,6 +133,35 @@ int ref_launch(int fmt, void* K, void* V, void* scK, void* scV, void* q, void* o
     return 0;
 }
 
+// Speed bar: n back-to-back launch() calls of the reference (its decode kernel
+// and its combine, on the legacy default stream), rotating over `copies` caches
+// (K[i], V[i], scK[i], scV[i]), timed with CUDA events around all of them.
+// Returns the average ms per launch() in *ms; 0 on success.
+int ref_time_launches(int fmt, void* const* K, void* const* V, void* const* scK, void* const* scV, int copies,
+                      void* q, void* out, float* ws, int H, int L, int D, int S, int n, float* ms) {
+    cudaEvent_t e0, e1;
+    if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) return 1;
+    const auto bufs = [&](int i) {
+        DeviceBufs b;
+        b.K = K[i % copies]; b.V = V[i % copies];
+        b.scK = scK ? scK[i % copies] : nullptr; b.scV = scV ? scV[i % copies] : nullptr;
+        b.q = (__half*)q; b.out = (__half*)out; b.ws = ws;
+        return b;
+    };
+    for (int i = 0; i < 3; ++i) launch(fmt_from_int(fmt), bufs(i), H, L, D, S);
+    if (cudaDeviceSynchronize() != cudaSuccess) return 2;
+    cudaEventRecord(e0);
+    for (int i = 0; i < n; ++i) launch(fmt_from_int(fmt), bufs(i), H, L, D, S);
+    cudaEventRecord(e1);
+    if (cudaEventSynchronize(e1) != cudaSuccess) return 3;
+    float t = 0.f;
+    cudaEventElapsedTime(&t, e0, e1);
+    *ms = t / (float)n;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return cudaGetLastError() == cudaSuccess ? 0 : 4;
+}
+
 double ref_probe_ceiling() { return probe_ceiling(); }
 int ref_selftest() { return selftest(); }
 void ref_bench() { bench(); }

@@ -30,3 +30,20 @@ def golden():
         "selftest": np.load(os.path.join(g, "selftest_ref.npz")),
         "edge": np.load(os.path.join(g, "edge_quant.npz")),
     }
+
+
+@pytest.fixture(autouse=True)
+def _no_silent_device_errors(request):
+    """Every GPU test ends with the library's device error word clear: a
+    bounded wait that gave up inside a kernel fails the test that launched it
+    (tests that provoke one on purpose read and clear the word themselves)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None or "voltattn_b200" not in sys.modules:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    va = sys.modules["voltattn_b200"]
+    torch.cuda.synchronize()
+    err = va.device_error()
+    assert err == 0, f"a kernel of this test reported device error {err} (a bounded wait gave up)"

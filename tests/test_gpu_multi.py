@@ -1,8 +1,10 @@
 """Multi-GPU split-L decode on 2 GPUs (skipped with fewer): each rank holds a
 contiguous range of every head's KV positions, decodes it into partials, and
-the output is assembled (a) with an NCCL all-gather + the combine kernel and
-(b) with the fused peer-memory exchange (va_exchange_combine) over three
-consecutive steps; both must match the single-cache oracle reference."""
+the output is assembled (a) with an NCCL all-gather + the combine kernel,
+(b) with the peer-memory exchange kernel (va_exchange_combine) and (c) with
+the exchange fused into the decode (va_decode_splitl, one launch per step),
+over three consecutive steps; all must match the single-cache oracle
+reference."""
 import os
 import socket
 import tempfile
@@ -67,8 +69,10 @@ def _worker(rank, world, port, outdir):
         out_nccl = SplitL.decode(sl, pfn)
         out_p2p = torch.empty(H * D, dtype=torch.float16, device=dev)
         sl.decode_peer(pfn, out_p2p)
+        out_fused = torch.empty(H * D, dtype=torch.float16, device=dev)
+        sl.decode_fused(fmt, va.DeviceBufs(K, V, sKd, sVd, qd, out_fused, ws), S)
         torch.cuda.synchronize(dev)
-        for name, out in (("nccl", out_nccl), ("p2p", out_p2p)):
+        for name, out in (("nccl", out_nccl), ("p2p", out_p2p), ("fused", out_fused)):
             err = np.abs(out.float().cpu().numpy() - ref)
             results.append((name, step, bool((err <= ATOL + RTOL * np.abs(ref)).all()), float(err.max())))
     results.append(("device_error", -1, va.device_error() == 0, 0.0))

@@ -63,6 +63,10 @@ def _load():
     lib.va_exchange_buffer_bytes.argtypes = [i, i, i]; lib.va_exchange_buffer_bytes.restype = sz
     lib.va_exchange_combine.argtypes = [vp, i, i, i, i, C.POINTER(C.c_void_p), C.c_uint, vp, vp]
     lib.va_exchange_combine.restype = i
+    lib.va_decode_splitl.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, vp, sz, i, i, C.POINTER(C.c_void_p), C.c_uint,
+                                     vp]
+    lib.va_decode_splitl.restype = i
+    lib.va_set_peer_wait_limit.argtypes = [C.c_double]; lib.va_set_peer_wait_limit.restype = i
     lib.va_append_kv.argtypes = [i, vp, vp, vp, i, i, i, i, vp, vp]; lib.va_append_kv.restype = i
     lib.va_quantize_f8.argtypes = [vp, vp, vp, i, i, i, vp]; lib.va_quantize_f8.restype = i
     lib.va_copy_small.argtypes = [vp, vp, sz, vp]; lib.va_copy_small.restype = i
@@ -395,6 +399,23 @@ def exchange_combine(partial, H: int, D: int, R: int, rank: int, peer_ptrs, epoc
     arr = (C.c_void_p * R)(*peer_ptrs)
     _check(_lib.va_exchange_combine(_ptr(partial), H, D, R, rank, arr, epoch, _ptr(out), _stream_ptr(stream)),
            "exchange_combine")
+
+
+def decode_splitl(fmt, b: DeviceBufs, H: int, L: int, D: int, S: int, R: int, rank: int, peer_array, epoch: int,
+                  stream=None):
+    """Split-L step in one launch (include/voltattn.h, va_decode_splitl): this
+    rank's L positions per head, exchanged and merged with the other ranks'
+    into b.out. peer_array: a ctypes array of the R peer buffer addresses
+    (built once by the caller)."""
+    vb = b.va()
+    _check(_lib.va_decode_splitl(int(Fmt.parse(fmt)), C.byref(vb), H, L, D, S, _ptr(b.ws),
+                                 b.ws.numel() * b.ws.element_size(), R, rank, peer_array, epoch,
+                                 _stream_ptr(stream)), "decode_splitl")
+
+
+def set_peer_wait_limit(seconds: float) -> None:
+    """Bound of the split-L waits for the peers' partials (default 1 s)."""
+    _check(_lib.va_set_peer_wait_limit(float(seconds)), "set_peer_wait_limit")
 
 
 def device_error() -> int:

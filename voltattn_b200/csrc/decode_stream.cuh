@@ -41,6 +41,7 @@
 
 #include "formats.cuh"
 #include "lse_merge.cuh"
+#include "peer.cuh"
 
 namespace va {
 
@@ -77,6 +78,13 @@ struct DecodeParams {
     // KV stream are (query head, token) pairs, mq tokens per head; token i of
     // mq sees the stream's rows [0, len - (mq - 1 - i)) (1: plain decode)
     int mq;
+    // split-L across GPUs fused into the decode (xR > 0, tile kernel): the
+    // head's merged partial is exchanged with the other ranks over peer
+    // memory and the R partials merged into out (peer.cuh)
+    PeerBuffers x;
+    int xR, xrank;
+    unsigned xepoch;
+    unsigned long long xwait_ns;  // bound of the wait for the peers' partials
 };
 
 // G = query heads per KV head (1: the reference's batch-1 multi-head decode;

@@ -347,6 +347,13 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         pp = (pp >= 0 && pp < p.num_pages) ? pp : 0;
         return (pp * p.Hkv + g.hk) * p.page_rows + (yl - pg * p.page_rows);
     };
+    // a unit index from the schedule counter, nunits when none is left (also
+    // for any counter value, so a workspace that was not zeroed cannot send
+    // the producer outside the streams)
+    const auto next_unit = [&](unsigned* c, int n) -> int {
+        const unsigned v = atomicAdd(c, 1u);
+        return v < (unsigned)(n - (int)gridDim.x) ? (int)gridDim.x + (int)v : n;
+    };
     while (ok && u < nunits) {
         int unext = nunits;
         bool asked = false;
@@ -364,7 +371,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         if (cur < 0) {  // empty split: the header alone (slot and ticket still count)
             if (!waited && (k >= C::kStages || !asked)) ensure_wait();
             if (!asked) {
-                if (lane == 0) unext = (int)gridDim.x + (int)atomicAdd(&sched[0], 1u);
+                if (lane == 0) unext = next_unit(sched, nunits);
                 asked = true;
             }
             if (!acquire(k)) {
@@ -381,7 +388,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         for (int t = 0; cur >= 0; ++t, ++k) {
             if (!waited && (k >= C::kStages || (!asked && t >= g.ntiles - 2))) ensure_wait();
             if (!asked && t >= g.ntiles - 2) {
-                if (lane == 0) unext = (int)gridDim.x + (int)atomicAdd(&sched[0], 1u);
+                if (lane == 0) unext = next_unit(sched, nunits);
                 asked = true;
             }
             if (!acquire(k)) {
@@ -986,7 +993,8 @@ __device__ __forceinline__ void tc_merge_slots(const float* hs, int S, int D, in
 // (release, CTA scope); the wait on tdone acquires them; the gpu-scope
 // acquire-release ticket is cumulative over them.
 template <class C>
-__device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* tdone, uint64_t* tfree) {
+__device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* tdone, uint64_t* tfree,
+                               volatile int* shok) {
     constexpr int D = C::kD;
     const int lane = threadIdx.x & 31;
     for (int n = 0;; ++n) {
@@ -1008,6 +1016,14 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
                 const size_t hq = (size_t)h * C::kG + kq;
                 float ms, ls, od[D / 32];
                 tc_merge_slots<D / 32>(p.ws + hq * p.S * (D + 2), p.S, D, lane, ms, ls, od);
+                if (p.xR > 0) {  // split-L across GPUs: exchange, merge the ranks' partials, write out
+                    if (peer_exchange_head<D / 32>(p.x, p.xR, p.xrank, p.xepoch, p.xwait_ns, p.H * C::kG, D, (int)hq, ms, ls,
+                                                   od, lane, 32, lane, [] { __syncwarp(); }, shok)) {
+#pragma unroll
+                        for (int j = 0; j < D / 32; ++j) p.out[hq * D + lane + 32 * j] = __float2half_rn(od[j]);
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < D / 32; ++j) {
                     const int d = lane + 32 * j;
@@ -1077,6 +1093,11 @@ __global__ void __launch_bounds__(C::kThreads, 2)
     // preceding kernel may have written). With kTcEarlyKv the producer streams
     // the first stages of K/V first, which no decode writes, and waits before
     // it reads the query or touches the schedule counters.
+#ifdef VA_TC_TIMELINE
+    // timeline: 13 the first stage landed (seen by the idle ticket warp, before its grid wait)
+    if (kTcEarlyKv && warp == C::kWarps + 1 && lane == 0 && mbar_wait_bounded(&full[0], 0))
+        VA_TL(13, global_timer_ns());
+#endif
     if (warp != C::kWarps || !kTcEarlyKv) grid_dependency_wait();
     if (threadIdx.x == 0) grid_launch_dependents();
     if (threadIdx.x == 0) {  // timeline: 0 start, 1 SM
@@ -1097,7 +1118,7 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         return;
     }
     if (warp == C::kWarps + 1) {
-        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree);
+        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1);
         return;
     }
 

@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         return;
     }
     if (warp == C::kWarps + 1) {
-        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree);
+        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1);
         return;
     }
 

@@ -17,29 +17,13 @@
 // and leaves the head's output untouched.
 #pragma once
 
-#include "common.cuh"
+#include "peer.cuh"
 
 namespace va {
 
-constexpr int kMaxRanks = 8;
-
-struct PeerBuffers {
-    float* gather[kMaxRanks];     // rank r's gather buffer [2][R][H][D+2]
-    unsigned* flags[kMaxRanks];   // rank r's flags [2][R][H]
-};
-
-__device__ __forceinline__ void store_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned load_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __global__ void __launch_bounds__(128) exchange_combine_kernel(const float* __restrict__ partial, int H, int D,
                                                                int R, int rank, PeerBuffers peers, unsigned epoch,
-                                                               __half* __restrict__ out) {
+                                                               uint64_t wait_ns, __half* __restrict__ out) {
     const int h = blockIdx.x, tid = threadIdx.x;
     const int par = (int)(epoch & 1u);
     const size_t slot_f = (size_t)(D + 2);
@@ -65,7 +49,7 @@ __global__ void __launch_bounds__(128) exchange_combine_kernel(const float* __re
             const uint64_t t0 = global_timer_ns();
             for (uint32_t i = 1; !seen; ++i) {
                 seen = load_acquire_sys(f) == epoch;
-                if (!seen && (i & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) break;
+                if (!seen && (i & 63u) == 0 && global_timer_ns() - t0 > wait_ns) break;
             }
         }
         if (!seen) {

@@ -3,6 +3,7 @@
 // entry point either launches its kernels or returns an error status.
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdlib>
 #include <cstring>
@@ -99,6 +100,11 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.page_rows = 0;
     p.num_pages = 0;
     p.mq = 1;
+    std::memset(&p.x, 0, sizeof(p.x));
+    p.xR = 0;
+    p.xrank = 0;
+    p.xepoch = 0;
+    p.xwait_ns = 0;
     return p;
 }
 
@@ -185,6 +191,8 @@ struct HostStepGraph {
 };
 constexpr size_t kHostStepGraphs = 16;  // cached graphs (oldest evicted)
 std::mutex g_host_step_mu;
+// Wall-clock bound of the split-L peer waits (va_set_peer_wait_limit).
+std::atomic<unsigned long long> g_peer_wait_ns{kWaitLimitNs};
 std::vector<HostStepGraph> g_host_steps;
 
 extern "C" {
@@ -314,6 +322,12 @@ int va_combine_partials(const float* slots, int R, int H, int S, int D, void* ou
     return VA_OK;
 }
 
+int va_set_peer_wait_limit(double seconds) {
+    if (!(seconds > 0.0) || seconds > 60.0) return VA_ERR_INVALID;
+    g_peer_wait_ns.store((unsigned long long)(seconds * 1e9));
+    return VA_OK;
+}
+
 size_t va_exchange_buffer_bytes(int R, int H, int D) {
     if (R < 1 || R > kMaxRanks || H < 1 || D < 1) return 0;
     const size_t g = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
@@ -332,10 +346,39 @@ int va_exchange_combine(const float* partial, int H, int D, int R, int rank, voi
         pb.gather[r] = static_cast<float*>(peer_buffers[r]);
         pb.flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[r]) + goff);
     }
-    exchange_combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(partial, H, D, R, rank, pb, epoch,
-                                                                              static_cast<__half*>(out));
+    exchange_combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        partial, H, D, R, rank, pb, epoch, g_peer_wait_ns.load(), static_cast<__half*>(out));
     VA_CUDA(cudaGetLastError());
     return VA_OK;
+}
+
+int va_decode_splitl(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes, int R,
+                     int rank, void* const* peer_buffers, unsigned epoch, void* stream) {
+    if (!peer_buffers || R < 1 || R > kMaxRanks || rank < 0 || rank >= R || epoch == 0) return VA_ERR_INVALID;
+    int rc = check_decode_args(fmt, bufs, H, L, D, S);
+    if (rc) return rc;
+    const Kind kind = fmt == VA_Q4P ? Kind::Q4 : fmt == VA_Q8P ? Kind::Q8 : Kind::Q3;
+    if ((fmt != VA_Q4P && fmt != VA_Q8P && fmt != VA_Q3P) || D != 128 || pick_consumer(kind, D, 1) != Consumer::kTc)
+        return VA_ERR_UNSUPPORTED;
+    if ((long long)H * L >= (1ll << 31)) return VA_ERR_TOO_LARGE;
+    if ((reinterpret_cast<uintptr_t>(bufs->q) & 15u) != 0) return VA_ERR_ALIGN;  // the query is bulk-copied
+    if (!ws || !aligned16(ws) || ws_bytes < va_workspace_bytes(H, D, S)) return VA_ERR_WORKSPACE;
+    unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
+    DecodeParams p = make_params(bufs, H, L, S, static_cast<float*>(ws), counters, kOutHalf, nullptr);
+    const size_t goff = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
+    for (int r = 0; r < R; ++r) {
+        if (!peer_buffers[r] || !aligned16(peer_buffers[r])) return VA_ERR_INVALID;
+        p.x.gather[r] = static_cast<float*>(peer_buffers[r]);
+        p.x.flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[r]) + goff);
+    }
+    p.xR = R;
+    p.xrank = rank;
+    p.xepoch = epoch;
+    p.xwait_ns = g_peer_wait_ns.load();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (fmt == VA_Q4P) return launch_tc<TcCfg<Kind::Q4, 128>>(p, st);
+    if (fmt == VA_Q8P) return launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
+    return launch_tc<TcCfg<Kind::Q3, 128>>(p, st);
 }
 
 int va_quantize(int bits, const float* x, void* codes, void* scales, int H, int L, int D, void* stream) {

@@ -127,6 +127,20 @@ class SplitLPeer(SplitL):
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
 
+    def decode_fused(self, fmt: str, bufs, S: int, stream=None) -> torch.Tensor:
+        """One launch per step (va_decode_splitl): the local decode of this
+        rank's positions with the peer exchange and merge fused into it;
+        bufs.K/V/scales hold this rank's local_len rows per head, the merged
+        fp16 output lands in bufs.out on every rank."""
+        import ctypes
+        import voltattn_b200 as va
+        if not hasattr(self, "_peer_array"):
+            self._peer_array = (ctypes.c_void_p * self.world)(*self.peer_ptrs)
+        self.epoch += 1
+        va.decode_splitl(fmt, bufs, self.H, self.local_len, self.D, S, self.world, self.rank, self._peer_array,
+                         self.epoch, stream)
+        return bufs.out
+
     def decode_peer(self, partial_fn: Callable[[int, int], torch.Tensor], out: torch.Tensor, stream=None) -> torch.Tensor:
         import voltattn_b200 as va
         partial = partial_fn(self.j0, self.j1)
