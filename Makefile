@@ -33,10 +33,20 @@ $(CLI): $(CSRC)/cli/voltattn_main.cu $(LIB) $(HDRS)
 	$(NVCC) -O3 -std=c++17 $(ARCH) -o $@ $(CSRC)/cli/voltattn_main.cu -Lvoltattn_b200 -lvoltattn_b200 \
 	  -Xlinker -rpath,'$$ORIGIN/..'
 
+# Development build with the tile kernel's per-CTA %globaltimer timeline
+# (-DVA_TC_TIMELINE), used by `python bench.py --timeline`; not the product.
+TLDIR     := voltattn_b200/_build/timeline
+timeline: $(OBJS)
+	@mkdir -p $(TLDIR)/voltattn_b200
+	$(NVCC) $(NVFLAGS) -rdc=true -DVA_TC_TIMELINE -c -o $(TLDIR)/launch_tc.o $(CSRC)/launch_tc.cu 2> $(TLDIR)/ptxas.log
+	$(NVCC) $(ARCH) -shared -rdc=true -o $(TLDIR)/voltattn_b200/libvoltattn_b200.so \
+	  $(filter-out $(OBJDIR)/launch_tc.o,$(OBJS)) $(TLDIR)/launch_tc.o -lcuda
+	cp voltattn_b200/__init__.py voltattn_b200/launcher.py $(TLDIR)/voltattn_b200/
+
 oracle:
 	$(MAKE) -C oracle REF_SRC="$(REF_SRC)"
 
 clean:
 	rm -rf $(LIB) $(CLI) voltattn_b200/ptxas.log voltattn_b200/link.log $(OBJDIR)
 
-.PHONY: all oracle clean
+.PHONY: all oracle clean timeline

@@ -75,6 +75,8 @@ def parse_args():
                     help="profiling driver for ncu: W+K plain launches of --fmt at --L (one cache, no graphs)")
     ap.add_argument("--prefill-lq", type=int, default=0,
                     help="with --profile: prefill of this many tokens (cache of --L rows, 32/8 heads) instead")
+    ap.add_argument("--timeline", action="store_true",
+                    help="per-CTA event timeline of the tile kernel (needs `make timeline`)")
     ap.add_argument("--gqa-batch", type=int, default=0,
                     help="with --profile: the batched GQA decode of config 5 with this many sequences instead")
     return ap.parse_args()
@@ -877,6 +879,62 @@ def run_ours(args, rank, world):
         dist.destroy_process_group()
 
 
+def run_timeline(args):
+    """Per-CTA event timeline of the tile kernel (the library built by `make
+    timeline`, -DVA_TC_TIMELINE): for --fmt at --L (and L=1024), one decode
+    after a decode of another cache copy (single: synchronised between them)
+    and the last of three back-to-back decodes (b2b). Times in us from the
+    first CTA's start: CTA start, producer start, stages 0..3 landed (as the
+    consumers see them), last tile consumed, consumers done, ticket warp done,
+    the last head's merge written. Percentiles 0/10/50/90/100 over CTAs."""
+    import ctypes
+    tl = os.path.join(ROOT, "voltattn_b200", "_build", "timeline")
+    if not os.path.exists(os.path.join(tl, "voltattn_b200", "libvoltattn_b200.so")):
+        sys.exit("build it first: make timeline")
+    sys.path.insert(0, tl)
+    import torch
+    import voltattn_b200 as va
+    lib = va.lib()
+    lib.va_debug_tc_timeline.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    dev = torch.device("cuda", 0)
+    buf = np.zeros(1024 * 16, dtype=np.uint64)
+    slots = {"start": 0, "producer_start": 11, "stage0": 2, "stage1": 8, "stage2": 9, "stage3": 10,
+             "last_tile": 3, "consumers_done": 7, "ticket_done": 4}
+    res = {}
+    for L in sorted({1024, args.L}):
+        caches = [make_cache(va, torch, args.fmt, L, 99 + i, dev) for i in range(3)]
+        q = torch.randn(H * D, device=dev).half()
+        out = torch.empty(H * D, dtype=torch.float16, device=dev)
+        S = va.suggest_splits(args.fmt, H, L, D)
+        ws = va.new_workspace(H, D, S, dev)
+        bs = [va.DeviceBufs(*c, q, out, ws) for c in caches]
+        torch.cuda.synchronize(dev)
+        for mode in ("single", "b2b"):
+            for _ in range(4):
+                va.launch(args.fmt, bs[0], H, L, D, S)
+                if mode == "single":
+                    torch.cuda.synchronize(dev)
+                va.launch(args.fmt, bs[1], H, L, D, S)
+                if mode == "b2b":
+                    va.launch(args.fmt, bs[2], H, L, D, S)
+                torch.cuda.synchronize(dev)
+                lib.va_debug_tc_timeline(buf.ctypes.data, buf.nbytes)
+            t = buf.reshape(1024, 16).astype(np.int64)
+            t = t[: int((t[:, 0] > 0).sum())]
+            t0 = t[:, 0].min()
+            r = {"ctas": len(t), "splits": S}
+            for name, c in slots.items():
+                v = t[:, c]
+                if (v > 0).all():
+                    r[name] = np.percentile((v - t0) / 1e3, [0, 10, 50, 90, 100]).round(2).tolist()
+            m = t[:, 5][t[:, 5] > 0]
+            r["last_merge"] = round(float((m.max() - t0) / 1e3), 2) if len(m) else None
+            res[f"{args.fmt} L={L} {mode}"] = r
+        del caches, bs
+        torch.cuda.empty_cache()
+    print(json.dumps({"timeline": res, "device_error": va.device_error()}), flush=True)
+
+
 def run_profile(args):
     """Small fixed workload for ncu captures: W warm-up then K decodes of one
     cache (size it above the 126 MB L2 with --L)."""
@@ -917,6 +975,9 @@ def run_profile(args):
 
 def main():
     args = parse_args()
+    if args.timeline:
+        run_timeline(args)
+        return
     if args.profile:
         run_profile(args)
         return
