@@ -605,24 +605,29 @@ def prefill_flops(Hq, L, Lq):
     return 4.0 * D * Hq * pairs
 
 
-def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=10):
+def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=10, staged=True):
     """Prompt prefill on the tcgen05 kernel: Lq tokens over a cache of L rows
     (L = Lq: a fresh prompt), 32 query / 8 KV heads. TFLOP/s of the causal
     work (no flops counted for masked pairs), against the measured bf16 dense
-    peak (the kernel computes fp16 x fp16 -> fp32)."""
+    peak (the kernel computes fp16 x fp16 -> fp32). staged: the cache is
+    converted once to fp16 in a workspace and the tiles move by tensor copies
+    (the conversion pass is inside the timed launches); unstaged: every CTA
+    converts the blocks it reads."""
     b = make_prefill(va, torch, dev, fmt, Hq, Hkv, L, Lq, 5150)
+    if staged:
+        b.ws = torch.empty(va.prefill_workspace_bytes(Hkv, L, D), dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize(dev)  # inputs made on the default stream are complete
     with torch.cuda.stream(stream):
         for _ in range(3):
-            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream)
+            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream, staged=staged)
     torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(reps):
-            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream)
+            va.prefill(fmt, b, Hq, Hkv, L, Lq, D, stream, staged=staged)
         e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / reps
@@ -630,7 +635,8 @@ def prefill_leg(va, torch, dev, fmt="q4+", Hq=32, Hkv=8, L=8192, Lq=8192, reps=1
     peaks, kind = measured_peaks()
     tf = flops / (ms * 1e9)
     err = va.device_error()
-    return {"workload": f"prefill Hq={Hq} Hkv={Hkv} D={D} L={L} Lq={Lq} causal {fmt}", "ms": ms,
+    return {"workload": f"prefill Hq={Hq} Hkv={Hkv} D={D} L={L} Lq={Lq} causal {fmt}"
+                        + ("" if staged else ", unstaged (per-CTA conversion)"), "ms": ms,
             "tok_s": Lq * 1e3 / ms, "tflops": tf, "flops": flops,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tf / peaks["bf16_tflops"], "peak_kind": f"{kind} (cuBLAS bf16 burst)"},
@@ -753,16 +759,49 @@ def splitl_leg(va, torch, dev, dist, world, steps, fmt="q4+", L=131072, S=None):
     err_nccl, ok_nccl = check(got_nccl)
     err_p2p, ok_p2p = check(got_p2p)
     err_fused, ok_fused = check(got_fused)
+    def timed_graph(n=100):
+        # the one-launch step counts its epochs on the device, so n steps go
+        # into one CUDA graph; every rank replays its own graph, the steps
+        # pair up through the peer flags
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            for _ in range(5):
+                sl.decode_fused(fmt, bf, S, st)
+        torch.cuda.synchronize(dev)
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=st):
+            for _ in range(n):
+                sl.decode_fused(fmt, bf, S, st)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            gph.replay()
+            e1.record(st)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / n], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     ms_nccl, n = timed(lambda: SplitL.decode(sl, pfn))
     ms_p2p, _ = timed(lambda: sl.decode_peer(pfn, out))
-    ms_fused, _ = timed(lambda: sl.decode_fused(fmt, bf, S))
+    ms_fused_eager, _ = timed(lambda: sl.decode_fused(fmt, bf, S))
+    ms_fused = timed_graph()
+    err_graph, ok_graph = check(out_fused.float())  # the last replayed step's output
     return {"workload": f"split-L decode, one sequence, H={H} D={D} L={L} {fmt} over {world} GPUs",
             "ms": ms_fused, "tok_s": 1e3 / ms_fused, "gbs": algorithmic_bytes(fmt, L) / (ms_fused * 1e6),
             "exchange": "peer-memory exchange and merge fused into the decode (va_decode_splitl, 1 launch per step)",
-            "ms_peer_2launch": ms_p2p, "ms_nccl_allgather": ms_nccl, "steps": n, "scaling": "strong",
+            "timing": "fused steps replayed from a CUDA graph of 100 (max over ranks); the other variants are "
+                      "eager launches from Python",
+            "ms_fused_eager": ms_fused_eager, "ms_peer_2launch": ms_p2p, "ms_nccl_allgather": ms_nccl, "steps": n,
+            "scaling": "strong",
             "launches_per_step": 1, "local_rows_per_head": Lr, "splits": S,
             "parity": {"against": "1-GPU decode of the same seeded full cache", "tol": "2e-3 + 1e-3*|ref|",
-                       "max_err_fused": err_fused, "ok_fused": ok_fused, "max_err_peer": err_p2p, "ok_peer": ok_p2p,
+                       "max_err_fused": err_fused, "ok_fused": ok_fused, "max_err_fused_graph": err_graph,
+                       "ok_fused_graph": ok_graph, "max_err_peer": err_p2p, "ok_peer": ok_p2p,
                        "max_err_nccl": err_nccl, "ok_nccl": ok_nccl}}
 
 
@@ -832,6 +871,8 @@ def run_ours(args, rank, world):
             for pf in ("q4+", "f16+"):
                 extra[f"prefill_{pf}"] = prefill_leg(va, torch, dev, pf)
                 torch.cuda.empty_cache()
+            extra["prefill_q4+_unstaged"] = prefill_leg(va, torch, dev, "q4+", staged=False)
+            torch.cuda.empty_cache()
             for sf in ("q4+", "q3+"):
                 extra[f"splitl_config3_base_{sf}"] = splitl_base_leg(va, torch, dev, K, sf)
                 torch.cuda.empty_cache()
@@ -945,6 +986,7 @@ def run_profile(args):
     if args.prefill_lq > 0:
         Hq, Hkv, Lq = 32, 8, args.prefill_lq
         b = make_prefill(va, torch, dev, fmt, Hq, Hkv, max(L, Lq), Lq, 5150)
+        b.ws = torch.empty(va.prefill_workspace_bytes(Hkv, max(L, Lq), D), dtype=torch.uint8, device=dev)
         for _ in range(args.warmup + args.steps):
             va.prefill(fmt, b, Hq, Hkv, max(L, Lq), Lq, D)
         torch.cuda.synchronize()

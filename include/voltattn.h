@@ -167,8 +167,11 @@ VA_API int va_exchange_combine(const float* partial, int H, int D, int R, int ra
  * va_workspace_bytes(H, D, S)), and the CTA that completes head h exchanges
  * the head's partial with the other ranks through peer_buffers (as
  * va_exchange_combine: va_exchange_buffer_bytes(R, H, D) each, mapped into
- * this process, zeroed once; epoch = 1, 2, 3, ... the same on all ranks) and
- * writes the merged fp16 output [H][D] on every rank. q3+/q4+/q8+ at D = 128
+ * this process, zeroed once; epoch = 1, 2, 3, ... the same on all ranks, or
+ * epoch = 0 on every call: the library counts the steps in the buffer itself,
+ * so a sequence of calls can be captured in a CUDA graph and replayed; do
+ * not mix the two ways on one buffer) and writes the merged fp16 output
+ * [H][D] on every rank. q3+/q4+/q8+ at D = 128
  * on the tile kernel; other formats return VA_ERR_UNSUPPORTED (use
  * va_decode_partial + va_exchange_combine). Waits are bounded (~1 s, then
  * va_device_error = peer wait). */
@@ -265,6 +268,20 @@ VA_API int va_prefill(int fmt, const va_bufs* bufs, int Hq, int Hkv, int L, int 
  * (VA_ERR_UNSUPPORTED). */
 VA_API int va_prefill_paged(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, int page_rows,
                             int num_pages, int Hq, int Hkv, int L, int Lq, int D, void* stream);
+
+/* va_prefill / va_prefill_paged with a workspace (no reference counterpart):
+ * the cache rows [0, L) of every KV head are first converted once to fp16 in
+ * ws (the same values the kernel above makes per block), then the attention
+ * moves K/V tiles by tensor copies instead of converting them in every CTA
+ * that reads them. ws: 16-byte aligned, ws_bytes >= va_prefill_workspace_bytes
+ * (2 * Hkv * L rounded up to 128 * D * 2 bytes); its contents need no
+ * initialisation. Same formats, shapes and results as va_prefill. */
+VA_API size_t va_prefill_workspace_bytes(int Hkv, int L, int D);
+VA_API int va_prefill_ws(int fmt, const va_bufs* bufs, int Hq, int Hkv, int L, int Lq, int D, void* ws,
+                         size_t ws_bytes, void* stream);
+VA_API int va_prefill_paged_ws(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, int page_rows,
+                               int num_pages, int Hq, int Hkv, int L, int Lq, int D, void* ws, size_t ws_bytes,
+                               void* stream);
 
 /* Multi-query decode (no reference counterpart), e.g. verifying Q speculative
  * tokens: the Q new tokens of each sequence are already appended to the cache

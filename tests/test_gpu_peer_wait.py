@@ -86,11 +86,15 @@ def test_fused_splitl_single_rank_matches_decode(va, fmt):
     V, sV = va.quantize(torch.randn(H * L * D, device="cuda", generator=g), bits, H, L, D)
     bufs = _buffers(va, 1, H, D)
     arr = (C.c_void_p * 1)(bufs[0].data_ptr())
-    for epoch in (1, 2, 3):  # both parity halves, then the first again
+    # host-counted steps: both parity halves, then the first again; then a
+    # fresh buffer with device-counted steps (epoch 0)
+    fresh = _buffers(va, 1, H, D)
+    arr0 = (C.c_void_p * 1)(fresh[0].data_ptr())
+    for epoch, a in ((1, arr), (2, arr), (3, arr), (0, arr0), (0, arr0), (0, arr0)):
         q = torch.randn(H * D, device="cuda", generator=g).half()
         want = va.decode(fmt, K, V, sK, sV, q, H, L, D, S).float()
         out = torch.full((H * D,), float("nan"), dtype=torch.float16, device="cuda")
-        va.decode_splitl(fmt, va.DeviceBufs(K, V, sK, sV, q, out, va.new_workspace(H, D, S)), H, L, D, S, 1, 0, arr,
+        va.decode_splitl(fmt, va.DeviceBufs(K, V, sK, sV, q, out, va.new_workspace(H, D, S)), H, L, D, S, 1, 0, a,
                          epoch)
         err = (out.float() - want).abs()
         assert bool((err <= 2e-3 + 1e-3 * want.abs()).all()), (fmt, epoch, float(err.max()))

@@ -62,8 +62,9 @@ def cache_for(oracle, fmt, kx, vx, rows, D, L):
     return kc, vc, ks, vs, oracle.dequant(kc, ks, 1, rows, D, bits), oracle.dequant(vc, vs, 1, rows, D, bits)
 
 
+@pytest.mark.parametrize("staged", [True, False], ids=["staged", "unstaged"])
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "{}_Hq{}_Hkv{}_L{}_Lq{}".format(*c))
-def test_prefill(va, oracle, case):
+def test_prefill(va, oracle, case, staged):
     import torch
     fmt, Hq, Hkv, L, Lq = case
     D = 128
@@ -86,7 +87,7 @@ def test_prefill(va, oracle, case):
     out = torch.full((Hq * Lq * D,), float("nan"), dtype=torch.float16, device=dev)
     b = va.DeviceBufs(K, V, sK, sV, qd, out)
     for _ in range(2):
-        va.prefill(fmt, b, Hq, Hkv, L, Lq, D)
+        va.prefill(fmt, b, Hq, Hkv, L, Lq, D, staged=staged)
         torch.cuda.synchronize()
         got = out.float().cpu().numpy().reshape(Hq, Lq, D)
         err = np.abs(got - ref)
@@ -116,8 +117,9 @@ PAGED = [  # fmt, Hq, Hkv, L, Lq, page_rows
 ]
 
 
+@pytest.mark.parametrize("staged", [True, False], ids=["staged", "unstaged"])
 @pytest.mark.parametrize("case", PAGED, ids=lambda c: "{}_Hq{}_Hkv{}_L{}_Lq{}_P{}".format(*c))
-def test_prefill_paged(va, oracle, case):
+def test_prefill_paged(va, oracle, case, staged):
     """The contiguous case's cache scattered into a shuffled page pool whose
     unused pages carry nan scales (or nan fp16 rows): the output must match
     the oracle exactly as for the contiguous layout."""
@@ -160,7 +162,7 @@ def test_prefill_paged(va, oracle, case):
     qd = as_dev(q.ravel()).view(torch.float16)
     out = torch.full((Hq * Lq * D,), float("nan"), dtype=torch.float16, device="cuda")
     va.prefill_paged(fmt, va.DeviceBufs(Kd, Vd, sKd, sVd, qd, out), as_dev(table), max_pages, P, num_pages, Hq, Hkv,
-                     L, Lq, D)
+                     L, Lq, D, staged=staged)
     torch.cuda.synchronize()
     got = out.float().cpu().numpy().reshape(Hq, Lq, D)
     err = np.abs(got - ref)

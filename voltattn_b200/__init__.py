@@ -79,6 +79,11 @@ def _load():
     lib.va_decode_multiquery.restype = i
     lib.va_prefill.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, i, vp]
     lib.va_prefill.restype = i
+    lib.va_prefill_workspace_bytes.argtypes = [i, i, i]; lib.va_prefill_workspace_bytes.restype = sz
+    lib.va_prefill_ws.argtypes = [i, C.POINTER(VaBufs), i, i, i, i, i, vp, sz, vp]
+    lib.va_prefill_ws.restype = i
+    lib.va_prefill_paged_ws.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, i, vp, sz, vp]
+    lib.va_prefill_paged_ws.restype = i
     lib.va_prefill_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, i, i, i, i, i, i, i, vp]
     lib.va_prefill_paged.restype = i
     lib.va_decode_paged.argtypes = [i, C.POINTER(VaBufs), vp, i, vp, i, i, i, i, i, i, i, vp, sz, vp]
@@ -340,22 +345,51 @@ def decode_multiquery(fmt, b: DeviceBufs, lens, B: int, Hq: int, Hkv: int, Q: in
            "decode_multiquery")
 
 
-def prefill(fmt, b: DeviceBufs, Hq: int, Hkv: int, L: int, Lq: int, D: int, stream=None):
+def prefill_workspace_bytes(Hkv: int, L: int, D: int) -> int:
+    return int(_lib.va_prefill_workspace_bytes(Hkv, L, D))
+
+
+def _prefill_ws(b: DeviceBufs, Hkv: int, L: int, D: int, staged: bool):
+    """The staging workspace: b.ws when it is large enough, else a new one;
+    None for the unstaged kernel."""
+    if not staged:
+        return None
+    need = prefill_workspace_bytes(Hkv, L, D)
+    if b.ws is not None and b.ws.numel() * b.ws.element_size() >= need:
+        return b.ws
+    import torch
+    return torch.empty(need, dtype=torch.uint8, device=b.q.device)
+
+
+def prefill(fmt, b: DeviceBufs, Hq: int, Hkv: int, L: int, Lq: int, D: int, stream=None, staged: bool = True):
     """Attention of the Lq new tokens of one sequence over its cache (the
     tokens' rows are its last Lq rows; token i sees rows [0, L - Lq + i]) on
     the tcgen05 tensor cores. b.K / b.V: [Hkv][L] rows; b.q, b.out: fp16
-    [Hq][Lq][D]; b.ws unused."""
+    [Hq][Lq][D]. staged (default): the cache is converted once into a
+    workspace (b.ws if large enough, else allocated) and the tiles move by
+    tensor copies (va_prefill_ws); staged=False: va_prefill, no workspace."""
     vb = b.va()
-    _check(_lib.va_prefill(int(Fmt.parse(fmt)), C.byref(vb), Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill")
+    ws = _prefill_ws(b, Hkv, L, D, staged)
+    if ws is None:
+        _check(_lib.va_prefill(int(Fmt.parse(fmt)), C.byref(vb), Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill")
+    else:
+        _check(_lib.va_prefill_ws(int(Fmt.parse(fmt)), C.byref(vb), Hq, Hkv, L, Lq, D, _ptr(ws),
+                                  ws.numel() * ws.element_size(), _stream_ptr(stream)), "prefill")
 
 
 def prefill_paged(fmt, b: DeviceBufs, block_table, max_pages: int, page_rows: int, num_pages: int, Hq: int,
-                  Hkv: int, L: int, Lq: int, D: int, stream=None):
+                  Hkv: int, L: int, Lq: int, D: int, stream=None, staged: bool = True):
     """prefill over a paged cache: b.K / b.V (and scales) are the page pool
     [num_pages][Hkv][page_rows], block_table int32 [max_pages] (CUDA)."""
     vb = b.va()
-    _check(_lib.va_prefill_paged(int(Fmt.parse(fmt)), C.byref(vb), _ptr(block_table), max_pages, page_rows, num_pages,
-                                 Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill_paged")
+    ws = _prefill_ws(b, Hkv, L, D, staged)
+    if ws is None:
+        _check(_lib.va_prefill_paged(int(Fmt.parse(fmt)), C.byref(vb), _ptr(block_table), max_pages, page_rows,
+                                     num_pages, Hq, Hkv, L, Lq, D, _stream_ptr(stream)), "prefill_paged")
+    else:
+        _check(_lib.va_prefill_paged_ws(int(Fmt.parse(fmt)), C.byref(vb), _ptr(block_table), max_pages, page_rows,
+                                        num_pages, Hq, Hkv, L, Lq, D, _ptr(ws), ws.numel() * ws.element_size(),
+                                        _stream_ptr(stream)), "prefill_paged")
 
 
 def decode_paged(fmt, b: DeviceBufs, block_table, max_pages: int, lens, B: int, Hq: int, Hkv: int, page_rows: int,

@@ -2,6 +2,7 @@
 // mbarrier and bulk-copy PTX, bounded waits, the device error word.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -105,6 +106,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         "%4;" ::"r"(smem_u32(dst_smem)),
         "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+// Brings a kernel-parameter tensor map into the descriptor cache ahead of its
+// first tensor copy.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
 // ---- named barriers (subset of the CTA's warps) ---------------------------

@@ -83,7 +83,8 @@ struct DecodeParams {
     // memory and the R partials merged into out (peer.cuh)
     PeerBuffers x;
     int xR, xrank;
-    unsigned xepoch;
+    unsigned xepoch;              // the step's epoch (1, 2, ...), or 0: read from *xepoch_ptr
+    unsigned* xepoch_ptr;         // this rank's epoch counter in its peer buffer (device-counted steps)
     unsigned long long xwait_ns;  // bound of the wait for the peers' partials
 };
 

@@ -190,9 +190,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
 
 __device__ __forceinline__ uint4 ldsm_x2_trans_b8(uint32_t addr) {
     uint4 r;
@@ -278,7 +275,7 @@ constexpr bool kTcEarlyKv = false;
 template <class C>
 __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const CUtensorMap* tmV, uint8_t* stages,
                             TcHeader* hdr, uint8_t* qring, uint64_t* full, uint64_t* empty, uint8_t* qfirst,
-                            uint64_t* qbar) {
+                            uint64_t* qbar, volatile unsigned* shep) {
     const int lane = threadIdx.x & 31;
     const uint64_t pol = l2_policy_evict_first();
     // the first unit's query goes to its own buffer ahead of the tiles, so the
@@ -296,8 +293,18 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         }
         __syncwarp();
     };
-    bool waited = !kTcEarlyKv;
-    if (waited) first_query();
+    // split-L across GPUs: the step's epoch, read once (after the grid
+    // dependency: the previous step's last CTA advanced the counter) and kept
+    // in shared memory for the ticket warp; the early-copy variant waits first
+    const auto read_epoch = [&]() {
+        if (p.xR > 0 && lane == 0)
+            *shep = p.xepoch_ptr ? *reinterpret_cast<volatile unsigned*>(p.xepoch_ptr) + 1u : p.xepoch;
+    };
+    bool waited = !kTcEarlyKv || p.xR > 0;
+    if (waited) {
+        read_epoch();
+        first_query();
+    }
     const auto ensure_wait = [&]() {
         if (!waited) {
             grid_dependency_wait();
@@ -536,6 +543,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
         if (lane == 0) {
             sched[0] = 0u;
             sched[1] = 0u;
+            if (p.xR > 0 && p.xepoch_ptr) *p.xepoch_ptr = *shep;  // this step's epoch, for the next step
         }
     }
     if (ok && acquire(k)) {
@@ -994,7 +1002,7 @@ __device__ __forceinline__ void tc_merge_slots(const float* hs, int S, int D, in
 // acquire-release ticket is cumulative over them.
 template <class C>
 __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* tdone, uint64_t* tfree,
-                               volatile int* shok) {
+                               volatile int* shok, const volatile unsigned* shep) {
     constexpr int D = C::kD;
     const int lane = threadIdx.x & 31;
     for (int n = 0;; ++n) {
@@ -1017,8 +1025,8 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
                 float ms, ls, od[D / 32];
                 tc_merge_slots<D / 32>(p.ws + hq * p.S * (D + 2), p.S, D, lane, ms, ls, od);
                 if (p.xR > 0) {  // split-L across GPUs: exchange, merge the ranks' partials, write out
-                    if (peer_exchange_head<D / 32>(p.x, p.xR, p.xrank, p.xepoch, p.xwait_ns, p.H * C::kG, D, (int)hq, ms, ls,
-                                                   od, lane, 32, lane, [] { __syncwarp(); }, shok)) {
+                    if (peer_exchange_head<D / 32>(p.x, p.xR, p.xrank, *shep, p.xwait_ns, p.H * C::kG, D, (int)hq,
+                                                   ms, ls, od, lane, 32, lane, [] { __syncwarp(); }, shok)) {
 #pragma unroll
                         for (int j = 0; j < D / 32; ++j) p.out[hq * D + lane + 32 * j] = __float2half_rn(od[j]);
                     }
@@ -1114,11 +1122,13 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
-        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar);
+        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar,
+                       reinterpret_cast<volatile unsigned*>(shFail + 2));
         return;
     }
     if (warp == C::kWarps + 1) {
-        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1);
+        if (p.out_mode != kOutSlots)
+            tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1, reinterpret_cast<volatile unsigned*>(shFail + 2));
         return;
     }
 

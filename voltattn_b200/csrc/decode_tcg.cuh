@@ -372,11 +372,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
-        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar);
+        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar,
+                       reinterpret_cast<volatile unsigned*>(shFail + 2));
         return;
     }
     if (warp == C::kWarps + 1) {
-        if (p.out_mode != kOutSlots) tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1);
+        if (p.out_mode != kOutSlots)
+            tc_ticket_warp<C>(p, th, tdone, tfree, shFail + 1, reinterpret_cast<volatile unsigned*>(shFail + 2));
         return;
     }
 

@@ -96,5 +96,20 @@ int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int row_by
     return r == CUDA_SUCCESS ? VA_OK : VA_ERR_UNSUPPORTED;
 }
 
+// fp16 rows of 128 elements ([rows][128], 256-byte stride), boxes of 64
+// elements (128 bytes, the 128-byte swizzle span) by box_rows rows.
+int encode_f16_rows_map(CUtensorMap* m, const void* base, long long rows, int box_rows) {
+    const auto enc = tensor_map_encoder();
+    if (!enc) return VA_ERR_UNSUPPORTED;
+    const cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {256};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VA_OK : VA_ERR_UNSUPPORTED;
+}
+
 }  // namespace host
 }  // namespace va

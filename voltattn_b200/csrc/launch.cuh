@@ -63,6 +63,13 @@ int launch_stream_fmt_g(int fmt, const DecodeParams& p, int D, cudaStream_t st);
 int stream_cfg_tile_rows(int fmt, int D);
 int stream_cfg_occupancy(int fmt, int D, int dev, int* occ);
 int launch_prefill_fmt(int fmt, const PrefillParams& p, cudaStream_t st);
+// Staged prefill: the cache converted once to fp16 rows in ws (prefill_stage_rows
+// rows per KV head), then the attention with tensor copies of the tiles.
+int prefill_stage_rows(int L);
+size_t prefill_stage_bytes(int Hkv, int L, int D);
+int launch_prefill_staged_fmt(int fmt, const PrefillParams& p, void* ws, cudaStream_t st);
+// fp16 [rows][128] tensor map, 64-element x box_rows boxes, 128-byte swizzle.
+int encode_f16_rows_map(CUtensorMap* m, const void* base, long long rows, int box_rows);
 
 }  // namespace host
 }  // namespace va

@@ -104,6 +104,7 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.xR = 0;
     p.xrank = 0;
     p.xepoch = 0;
+    p.xepoch_ptr = nullptr;
     p.xwait_ns = 0;
     return p;
 }
@@ -330,8 +331,10 @@ int va_set_peer_wait_limit(double seconds) {
 
 size_t va_exchange_buffer_bytes(int R, int H, int D) {
     if (R < 1 || R > kMaxRanks || H < 1 || D < 1) return 0;
+    // gather slots, flags, and a 256-byte block whose first word counts this
+    // rank's steps (va_decode_splitl with epoch 0)
     const size_t g = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
-    return g + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255);
+    return g + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255) + 256;
 }
 
 int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
@@ -354,7 +357,7 @@ int va_exchange_combine(const float* partial, int H, int D, int R, int rank, voi
 
 int va_decode_splitl(int fmt, const va_bufs* bufs, int H, int L, int D, int S, void* ws, size_t ws_bytes, int R,
                      int rank, void* const* peer_buffers, unsigned epoch, void* stream) {
-    if (!peer_buffers || R < 1 || R > kMaxRanks || rank < 0 || rank >= R || epoch == 0) return VA_ERR_INVALID;
+    if (!peer_buffers || R < 1 || R > kMaxRanks || rank < 0 || rank >= R) return VA_ERR_INVALID;
     int rc = check_decode_args(fmt, bufs, H, L, D, S);
     if (rc) return rc;
     const Kind kind = fmt == VA_Q4P ? Kind::Q4 : fmt == VA_Q8P ? Kind::Q8 : Kind::Q3;
@@ -374,6 +377,10 @@ int va_decode_splitl(int fmt, const va_bufs* bufs, int H, int L, int D, int S, v
     p.xR = R;
     p.xrank = rank;
     p.xepoch = epoch;
+    if (epoch == 0) {  // the step count lives in this rank's buffer, after the flags
+        const size_t eoff = goff + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255);
+        p.xepoch_ptr = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[rank]) + eoff);
+    }
     p.xwait_ns = g_peer_wait_ns.load();
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (fmt == VA_Q4P) return launch_tc<TcCfg<Kind::Q4, 128>>(p, st);
@@ -737,7 +744,7 @@ int va_decode_noalloc(int fmt, const va_bufs* bufs, int H, int L, int D, int S, 
 }
 
 static int prefill_impl(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, const int* block_table,
-                        int page_rows, int num_pages, void* stream) {
+                        int page_rows, int num_pages, void* stream, void* ws = nullptr, size_t ws_bytes = 0) {
     if (!is_valid_fmt(fmt) || !b) return VA_ERR_INVALID;
     if (Hq < 1 || Hkv < 1 || Hq % Hkv || Lq < 1 || L < Lq) return VA_ERR_INVALID;
     if (D != 128) return VA_ERR_UNSUPPORTED;
@@ -762,7 +769,34 @@ static int prefill_impl(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int L
     p.page_rows = page_rows;
     p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (ws) {  // staged: the cache converted once, tiles by tensor copies
+        if (!aligned16(ws) || ws_bytes < prefill_stage_bytes(Hkv, L, D)) return VA_ERR_WORKSPACE;
+        if ((long long)Hkv * prefill_stage_rows(L) >= (1ll << 31)) return VA_ERR_TOO_LARGE;
+        return launch_prefill_staged_fmt(fmt, p, ws, st);
+    }
     return launch_prefill_fmt(fmt, p, st);
+}
+
+size_t va_prefill_workspace_bytes(int Hkv, int L, int D) {
+    if (Hkv < 1 || L < 1 || D != 128) return 0;
+    return prefill_stage_bytes(Hkv, L, D);
+}
+
+int va_prefill_ws(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* ws, size_t ws_bytes,
+                  void* stream) {
+    if (!ws) return VA_ERR_WORKSPACE;
+    return prefill_impl(fmt, b, Hq, Hkv, L, Lq, D, nullptr, 0, 0, stream, ws, ws_bytes);
+}
+
+int va_prefill_paged_ws(int fmt, const va_bufs* b, const int* block_table, int max_pages, int page_rows,
+                        int num_pages, int Hq, int Hkv, int L, int Lq, int D, void* ws, size_t ws_bytes,
+                        void* stream) {
+    if (!ws) return VA_ERR_WORKSPACE;
+    if (!block_table || page_rows < 1 || num_pages < 1 || max_pages < 1) return VA_ERR_INVALID;
+    if (fmt == VA_Q4CP) return VA_ERR_UNSUPPORTED;  // its V scales are per sequence row, not paged
+    if ((long long)max_pages * page_rows < L) return VA_ERR_INVALID;
+    if ((long long)num_pages * Hkv * page_rows >= (1ll << 40)) return VA_ERR_TOO_LARGE;
+    return prefill_impl(fmt, b, Hq, Hkv, L, Lq, D, block_table, page_rows, num_pages, stream, ws, ws_bytes);
 }
 
 int va_prefill(int fmt, const va_bufs* b, int Hq, int Hkv, int L, int Lq, int D, void* stream) {

@@ -118,11 +118,17 @@ class SplitLPeer(SplitL):
         import voltattn_b200 as va
         self.H, self.D = H, D
         nbytes = va.exchange_buffer_bytes(self.world, H, D)
+        g = self.group if self.group is not None else dist.group.WORLD
+        # two buffers: host-counted steps (decode_peer) and device-counted
+        # steps (decode_fused); one buffer must not serve both ways
         self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
         self.buf.zero_()
-        g = self.group if self.group is not None else dist.group.WORLD
         self.handle = symm_mem.rendezvous(self.buf, g)
         self.peer_ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.fbuf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.fbuf.zero_()
+        self.fhandle = symm_mem.rendezvous(self.fbuf, g)
+        self.fused_ptrs = [int(p) for p in self.fhandle.buffer_ptrs]
         self.epoch = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
@@ -131,14 +137,15 @@ class SplitLPeer(SplitL):
         """One launch per step (va_decode_splitl): the local decode of this
         rank's positions with the peer exchange and merge fused into it;
         bufs.K/V/scales hold this rank's local_len rows per head, the merged
-        fp16 output lands in bufs.out on every rank."""
+        fp16 output lands in bufs.out on every rank. The steps are counted on
+        the device (epoch 0), so calls can be captured in a CUDA graph; this
+        object's buffers then serve only this path."""
         import ctypes
         import voltattn_b200 as va
         if not hasattr(self, "_peer_array"):
-            self._peer_array = (ctypes.c_void_p * self.world)(*self.peer_ptrs)
-        self.epoch += 1
-        va.decode_splitl(fmt, bufs, self.H, self.local_len, self.D, S, self.world, self.rank, self._peer_array,
-                         self.epoch, stream)
+            self._peer_array = (ctypes.c_void_p * self.world)(*self.fused_ptrs)
+        va.decode_splitl(fmt, bufs, self.H, self.local_len, self.D, S, self.world, self.rank, self._peer_array, 0,
+                         stream)
         return bufs.out
 
     def decode_peer(self, partial_fn: Callable[[int, int], torch.Tensor], out: torch.Tensor, stream=None) -> torch.Tensor:
