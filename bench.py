@@ -579,6 +579,52 @@ def gqa_leg(va, torch, dev, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lma
             "steps": n, "launches_per_step": 1}
 
 
+def gqa_sharded_leg(va, torch, dev, dist, world, rank, steps, seed=4242, fmt="q4+", B=64, Hq=32, Hkv=8, Lmax=32768,
+                    S=4):
+    """BASELINE config 5 sharded by sequence over the ranks (BatchSharding:
+    rank r decodes sequences [b0, b1) of the same seeded batch, no collective
+    on the data path). Each rank times a CUDA graph of back-to-back decodes of
+    its shard; tok/s = B / (max over ranks of the per-step time)."""
+    from voltattn_b200.launcher import split_range
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lens_all = torch.randint(1024, Lmax + 1, (B,), generator=g, dtype=torch.int32)
+    b0, b1 = split_range(B, world, rank, align=1)
+    Bl = b1 - b0
+    b, lens_d, nbytes = make_gqa(va, torch, dev, seed + 1 + rank, fmt, Bl, Hq, Hkv, Lmax, S)
+    lens_d = lens_all[b0:b1].to(dev)
+    nbytes = int(lens_all[b0:b1].sum()) * Hkv * 2 * (D * FORMAT_BITS[fmt] // 8 + 2 * (D // 64))
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            va.decode_gqa(fmt, b, lens_d, Bl, Hq, Hkv, Lmax, D, S, stream)
+    torch.cuda.synchronize(dev)
+    n = max(3, min(steps, 200))
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=stream):
+        for _ in range(n):
+            va.decode_gqa(fmt, b, lens_d, Bl, Hq, Hkv, Lmax, D, S, stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        gph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / n, float(nbytes)], device=dev, dtype=torch.float64)
+    tmax = t[:1].clone()
+    dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    tb = t[1:].clone()
+    dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+    ms = float(tmax.item())
+    return {"workload": f"batched GQA decode B={B} Hq={Hq} Hkv={Hkv} D={D} lens~U[1024,{Lmax}] {fmt}, "
+                        f"sequences sharded over {world} GPUs", "ms": ms, "tok_s": B * 1e3 / ms,
+            "gbs_total": float(tb.item()) / (ms * 1e6), "splits": S, "steps": n, "scaling": "strong",
+            "launches_per_step_per_rank": 1}
+
+
 def make_prefill(va, torch, dev, fmt, Hq, Hkv, L, Lq, seed):
     """One sequence's cache of L rows per KV head (its last Lq rows are the new
     tokens) in format fmt, quantized on the GPU, and the tokens' fp16 queries."""
@@ -885,6 +931,8 @@ def run_ours(args, rank, world):
             for sf in ("q4+", "q3+"):
                 extra[f"splitl_config3_{sf}"] = splitl_leg(va, torch, dev, dist, world, K, fmt=sf)
                 torch.cuda.empty_cache()
+            extra["gqa_config5_sharded"] = gqa_sharded_leg(va, torch, dev, dist, world, rank, K)
+            torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_leg(L, fmt)
