@@ -302,12 +302,14 @@ VA_API int va_decode_multiquery(int fmt, const va_bufs* bufs, const int* lens, i
  * head k of sequence b lives in page block_table[b * max_pages + j / page_rows]
  * (device int32 [B][max_pages]) at row j % page_rows. lens: device int32 [B],
  * 1 <= lens[b] <= max_pages * page_rows. Entries outside [0, num_pages) read
- * page 0 (decode) or skip the row (append). Supported: D = 128, page_rows a
- * multiple of 32, q3+ / q4+ / q8+ with Hq == Hkv and q4+ with Hq == 2, 4 or
- * 8 * Hkv (the tensor-core tile kernels); other shapes return
- * VA_ERR_UNSUPPORTED. q must be
- * 16-byte aligned. ws as for va_decode_gqa (va_gqa_workspace_bytes). Splits
- * s of a sequence take its 256-row tiles s, s + S, s + 2S, ... */
+ * page 0 (decode) or skip the row (append). Decode supports every "+" format
+ * but q4c+ at D = 64 or 128 with Hq / Hkv in {1, 2, 4, 8} and page_rows a
+ * multiple of 8: q3+ / q4+ / q8+ with Hq == Hkv and q4+ with Hq == 2, 4 or
+ * 8 * Hkv at D = 128 with page_rows a multiple of 32 run the tensor-core tile
+ * kernels (splits s of a sequence take its 256-row tiles s, s + S, s + 2S,
+ * ...); the rest the streaming / grouped-query kernels, which copy each run
+ * of rows inside one page. Other shapes return VA_ERR_UNSUPPORTED. q must be
+ * 16-byte aligned. ws as for va_decode_gqa (va_gqa_workspace_bytes). */
 VA_API int va_decode_paged(int fmt, const va_bufs* bufs, const int* block_table, int max_pages, const int* lens,
                            int B, int Hq, int Hkv, int page_rows, int num_pages, int D, int S, void* ws,
                            size_t ws_bytes, void* stream);

@@ -68,31 +68,64 @@ CASES = [  # fmt, B, Hq, Hkv, Lmax, page_rows, S
     ("q4+", 2, 8, 4, 500, 32, 2),    # 2 query heads per KV head
     ("q3+", 3, 4, 4, 777, 96, 3),
     ("q3+", 2, 2, 2, 1500, 32, 4),
+    # the streaming / grouped-query kernels (page rows a multiple of 8)
+    ("f16+", 3, 8, 2, 700, 64, 3),
+    ("bf16+", 2, 4, 4, 500, 24, 2),
+    ("f8+", 2, 8, 4, 900, 40, 3),
+    ("q8+", 2, 16, 4, 1031, 64, 2),   # 4 query heads per KV head
+    ("q3+", 3, 8, 2, 777, 96, 3),     # 4 query heads per KV head
+    ("q4+", 2, 4, 4, 600, 16, 2),     # pages too small for the tile kernel
+    ("q4+", 2, 8, 4, 700, 32, 2, 64),  # D = 64
+    ("q8+", 1, 2, 2, 333, 8, 1, 64),
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=lambda c: "{}_B{}_Hq{}_Hkv{}_L{}_P{}_S{}".format(*c))
+def _encode(oracle, x, rows, D, fmt):
+    """codes (uint8 rows), scales (uint16, or None) and the exactly decoded
+    values of x in fmt, by the oracle."""
+    if fmt == "f16+":
+        h = oracle.f2h(x)
+        return h.view(np.uint8), None, oracle.h2f(h)
+    if fmt == "bf16+":
+        b = oracle.f2bf(x)
+        return b.view(np.uint8), None, (b.astype(np.uint32) << 16).view(np.float32)
+    if fmt == "f8+":
+        c, s = oracle.quantize_f8(x, 1, rows, D)
+        return c, s, oracle.dequant_f8(c, s, 1, rows, D)
+    bits = BITS[fmt]
+    c, s = oracle.quantize(x, 1, rows, D, bits)
+    return c, s, oracle.dequant(c, s, 1, rows, D, bits)
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "{}_B{}_Hq{}_Hkv{}_L{}_P{}_S{}".format(*c[:7])
+                         + ("_D{}".format(c[7]) if len(c) > 7 else ""))
 def test_decode_paged(va, oracle, case):
     import torch
-    fmt, B, Hq, Hkv, Lmax, page_rows, S = case
-    D = 128
-    bits = BITS[fmt]
-    rng = np.random.default_rng(B * 7919 + Hq * 31 + Lmax + page_rows)
+    fmt, B, Hq, Hkv, Lmax, page_rows, S = case[:7]
+    D = case[7] if len(case) > 7 else 128
+    bits = {"f16+": 16, "bf16+": 16, "f8+": 8}.get(fmt) or BITS[fmt]
+    rng = np.random.default_rng(B * 7919 + Hq * 31 + Lmax + page_rows + D)
     lens = rng.integers(1, Lmax + 1, size=B).astype(np.int32)
     lens[0] = Lmax
     rows = B * Hkv * Lmax
     kx, vx, _ = oracle.gen_case(int(rng.integers(1 << 30)), 1, rows, D)
     q = oracle.f2h(rng.standard_normal(B * Hq * D).astype(np.float32))
-    kc, ks = oracle.quantize(kx, 1, rows, D, bits)
-    vc, vs = oracle.quantize(vx, 1, rows, D, bits)
-    ref = oracle.reference_gqa(oracle.dequant(kc, ks, 1, rows, D, bits), oracle.dequant(vc, vs, 1, rows, D, bits),
-                               q, lens, B, Hq, Hkv, Lmax, D)
+    kc, ks, kd = _encode(oracle, kx, rows, D, fmt)
+    vc, vs, vd = _encode(oracle, vx, rows, D, fmt)
+    ref = oracle.reference_gqa(kd, vd, q, lens, B, Hq, Hkv, Lmax, D)
     table, max_pages, num_pages = make_table(rng, lens, Lmax, page_rows, 5)
-    pkc, pks = build_pool(rng, kc, ks, lens, table, num_pages, Hkv, Lmax, D, bits, page_rows, np.nan)
-    pvc, pvs = build_pool(rng, vc, vs, lens, table, num_pages, Hkv, Lmax, D, bits, page_rows, np.inf)
+    if ks is None:  # no scales: unused rows hold random bit patterns (nan and inf among them)
+        pkc, _ = build_pool(rng, kc, np.zeros(rows * (D // 64), np.uint16), lens, table, num_pages, Hkv, Lmax, D,
+                            bits, page_rows, 0.0)
+        pvc, _ = build_pool(rng, vc, np.zeros(rows * (D // 64), np.uint16), lens, table, num_pages, Hkv, Lmax, D,
+                            bits, page_rows, 0.0)
+        pks = pvs = None
+    else:
+        pkc, pks = build_pool(rng, kc, ks, lens, table, num_pages, Hkv, Lmax, D, bits, page_rows, np.nan)
+        pvc, pvs = build_pool(rng, vc, vs, lens, table, num_pages, Hkv, Lmax, D, bits, page_rows, np.inf)
     K, V = torch.from_numpy(pkc).cuda(), torch.from_numpy(pvc).cuda()
-    sK = torch.from_numpy(pks).cuda().view(torch.float16)
-    sV = torch.from_numpy(pvs).cuda().view(torch.float16)
+    sK = None if pks is None else torch.from_numpy(pks).cuda().view(torch.float16)
+    sV = None if pvs is None else torch.from_numpy(pvs).cuda().view(torch.float16)
     qd = torch.from_numpy(q).cuda().view(torch.float16)
     out = torch.full((B * Hq * D,), float("nan"), dtype=torch.float16, device="cuda")
     ws = torch.zeros(va.gqa_workspace_bytes(B, Hq, D, S), dtype=torch.uint8, device="cuda")
@@ -149,7 +182,9 @@ def test_paged_rejects_unsupported(va):
     bt = torch.zeros(B * max_pages, dtype=torch.int32, device=dev)
     lens = torch.ones(B, dtype=torch.int32, device=dev)
     b = va.DeviceBufs(K, K, sK, sK, q, out, ws)
-    with pytest.raises(RuntimeError):  # page rows not a multiple of 32
-        va.decode_paged("q4+", b, bt, max_pages, lens, B, Hq, Hkv, page_rows, num_pages, D, 1)
-    with pytest.raises(RuntimeError):  # q3+ pages: one query head per KV head only
-        va.decode_paged("q3+", b, bt, max_pages, lens, B, 2 * Hq, Hkv, 32, num_pages, D, 1)
+    with pytest.raises(RuntimeError):  # page rows not a multiple of 8
+        va.decode_paged("q4+", b, bt, max_pages, lens, B, Hq, Hkv, 12, num_pages, D, 1)
+    with pytest.raises(RuntimeError):  # per-channel scales are per sequence, not paged
+        va.decode_paged("q4c+", b, bt, max_pages, lens, B, Hq, Hkv, 32, num_pages, D, 1)
+    with pytest.raises(RuntimeError):  # 3 query heads per KV head
+        va.decode_paged("q8+", b, bt, max_pages, lens, B, 3 * Hkv, Hkv, 32, num_pages, D, 1)

@@ -294,9 +294,12 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
     const long long nr8 = p.total_rows & ~7ll;
     const int nunits = p.H * p.S;
     int k = 0;
+    const bool paged = p.page_rows > 0;
     for (int u = unit_begin(nunits), ue = unit_begin(nunits, 1); u < ue; ++u) {
         const UnitGeom g = unit_geom<C>(p, u);
-        const long long cend = min((g.r1 + 7) & ~7ll, nr8);
+        // paged cache: logical rows of whole 8-row blocks are copied (a page
+        // holds whole blocks), so no row needs a plain load
+        const long long cend = paged ? (g.r1 + 7) & ~7ll : min((g.r1 + 7) & ~7ll, nr8);
         for (int t = 0; t < g.ntiles; ++t, ++k) {
             const int stage = k % C::kStages;
             const uint32_t ph = (uint32_t)(k / C::kStages) & 1u;
@@ -316,6 +319,35 @@ __device__ void stream_producer(const DecodeParams& p, uint8_t* smem, uint64_t* 
             const long long tend = t0 + C::kTr;
             const int brows = (int)max(0ll, min(tend, cend) - t0);
             const long long rg0 = max(t0, nr8), rg1 = min(tend, g.r1);
+            if (paged) {
+                // the tile's logical rows, one bulk copy per matrix and run of
+                // rows inside one page (rows and pages are whole 8-row
+                // blocks: every copy is 16-byte aligned and sized)
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[stage], (uint32_t)brows * (2u * C::kRb + 2u * C::kSb));
+                    const int b = g.h / p.Hkv, hk = g.h - b * p.Hkv;
+                    int j = (int)(t0 - (long long)g.h * p.L);  // sequence position (below 2^31)
+                    for (int dr = 0; dr < brows;) {
+                        const int pi = j / p.page_rows, in = j - pi * p.page_rows;
+                        const int n = min(brows - dr, p.page_rows - in);
+                        int pg = pi < p.max_pages ? __ldg(p.block_table + (size_t)b * p.max_pages + pi) : 0;
+                        pg = (pg >= 0 && pg < p.num_pages) ? pg : 0;
+                        const size_t ph = ((size_t)pg * p.Hkv + hk) * p.page_rows + in;
+                        bulk_g2s(sK + (size_t)dr * C::kRb, p.K + ph * C::kRb, (uint32_t)n * C::kRb, &full[stage], pol);
+                        bulk_g2s(sV + (size_t)dr * C::kRb, p.V + ph * C::kRb, (uint32_t)n * C::kRb, &full[stage], pol);
+                        if constexpr (C::kSb > 0) {
+                            bulk_g2s(sSK + (size_t)dr * C::kSb, reinterpret_cast<const uint8_t*>(p.scK) + ph * C::kSb,
+                                     (uint32_t)n * C::kSb, &full[stage], pol);
+                            bulk_g2s(sSV + (size_t)dr * C::kSb, reinterpret_cast<const uint8_t*>(p.scV) + ph * C::kSb,
+                                     (uint32_t)n * C::kSb, &full[stage], pol);
+                        }
+                        dr += n;
+                        j += n;
+                    }
+                }
+                __syncwarp();
+                continue;
+            }
             if (rg1 > rg0) {
                 // tail rows of the whole tensor: plain 8-byte / 2-byte loads
                 const int rrows = (int)(rg1 - rg0);

@@ -37,15 +37,17 @@ template <class C>
 int launch_stream(const DecodeParams& p, cudaStream_t st) {
     if constexpr (!is_float_kind(C::kKind)) {
         const Consumer c = pick_consumer(C::kKind, C::kD, C::kG);
+        // the tile kernels page in 32-row copy boxes
+        const bool tc_pages_ok = p.page_rows == 0 || p.page_rows % 32 == 0;
         if constexpr (C::kG == 1 && C::kD == 128 &&
                       (C::kKind == Kind::Q3 || C::kKind == Kind::Q4 || C::kKind == Kind::Q8)) {
             // tensor coordinates are 32-bit and the query is bulk-copied
-            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
+            if (c == Consumer::kTc && tc_pages_ok && p.total_rows < (1ll << 31) && p.counters &&
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tc<TcCfg<C::kKind, 128>>(p, st);
         }
         if constexpr ((C::kG == 2 || C::kG == 4 || C::kG == 8) && C::kD == 128 && C::kKind == Kind::Q4) {
-            if (c == Consumer::kTc && p.total_rows < (1ll << 31) && p.counters &&
+            if (c == Consumer::kTc && tc_pages_ok && p.total_rows < (1ll << 31) && p.counters &&
                 (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0)
                 return launch_tcg<TcgCfg<Kind::Q4, 128, C::kG>>(p, st);
         }

@@ -663,11 +663,15 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     // the tile kernels: q3+ / q4+ / q8+ with one query head per KV head, q4+
     // with 2, 4 or 8; copy boxes of 32 rows stay inside a page
     const Kind kind = fmt == VA_Q8P ? Kind::Q8 : fmt == VA_Q3P ? Kind::Q3 : Kind::Q4;
-    const bool ok = D == 128 && page_rows % 32 == 0 &&
+    const bool tc = D == 128 && page_rows % 32 == 0 &&
                     ((G == 1 && (fmt == VA_Q3P || fmt == VA_Q4P || fmt == VA_Q8P)) ||
                      ((G == 2 || G == 4 || G == 8) && fmt == VA_Q4P)) &&
                     pick_consumer(kind, D, G) == Consumer::kTc;
-    if (!ok) return VA_ERR_UNSUPPORTED;
+    // every other "+" format and shape: the streaming / mma kernels, whose
+    // producer copies each run of rows inside a page (whole 8-row blocks)
+    const bool streamed = !tc && (D == 64 || D == 128) && page_rows % 8 == 0 && !is_plain(fmt) &&
+                          fmt != VA_Q4CP && (G == 1 || G == 2 || G == 4 || G == 8);
+    if (!tc && !streamed) return VA_ERR_UNSUPPORTED;
     const long long streams = (long long)B * Hkv;
     const long long rows = (long long)num_pages * Hkv * page_rows;
     const long long lmax = (long long)max_pages * page_rows;
@@ -687,6 +691,14 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     p.page_rows = page_rows;
     p.num_pages = num_pages;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (streamed) {
+        switch (G) {
+            case 1: return launch_stream_fmt_g<1>(fmt, p, D, st);
+            case 2: return launch_stream_fmt_g<2>(fmt, p, D, st);
+            case 4: return launch_stream_fmt_g<4>(fmt, p, D, st);
+            default: return launch_stream_fmt_g<8>(fmt, p, D, st);
+        }
+    }
     if (G == 2) return launch_tcg<TcgCfg<Kind::Q4, 128, 2>>(p, st);
     if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
     if (G == 8) return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
