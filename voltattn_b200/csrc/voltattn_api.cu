@@ -100,6 +100,7 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.page_rows = 0;
     p.num_pages = 0;
     p.mq = 1;
+    p.q_mapped = 0;
     std::memset(&p.x, 0, sizeof(p.x));
     p.xR = 0;
     p.xrank = 0;
@@ -109,8 +110,18 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     return p;
 }
 
+// Whether va_decode's fused path runs the tensor-core tile kernel for this
+// shape (the kernel that can take a query in mapped host memory).
+bool decode_uses_tile_kernel(int fmt, int H, int L, int D, bool fused) {
+    if (!fused || D != 128 || (long long)H * L >= (1ll << 31)) return false;
+    if (fmt == VA_Q4CP) return true;
+    if (fmt != VA_Q4P && fmt != VA_Q8P && fmt != VA_Q3P) return false;
+    const Kind kind = fmt == VA_Q4P ? Kind::Q4 : fmt == VA_Q8P ? Kind::Q8 : Kind::Q3;
+    return pick_consumer(kind, D, 1) == Consumer::kTc;
+}
+
 int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws, size_t ws_bytes, float* partial,
-                void* stream) {
+                void* stream, int q_mapped = 0) {
     int rc = check_decode_args(fmt, b, H, L, D, S);
     if (rc) return rc;
     if (!ws || !aligned16(ws) || ws_bytes < slots_bytes(H, D, S)) return VA_ERR_WORKSPACE;
@@ -124,8 +135,8 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
         if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;
         if ((long long)H * L >= (1ll << 31)) return VA_ERR_TOO_LARGE;
         unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
-        const DecodeParams p =
-            make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+        DecodeParams p = make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+        p.q_mapped = q_mapped;
         return launch_tc<TcCfg<Kind::Q4, 128, true>>(p, st);
     }
     if (is_plain(fmt) || !fused_ok) {
@@ -146,8 +157,10 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
         return VA_OK;
     }
     unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
-    const DecodeParams p =
-        make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+    DecodeParams p = make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
+    // a mapped-host query only where the tile kernel runs (its producer loads it)
+    p.q_mapped = q_mapped && decode_uses_tile_kernel(fmt, H, L, D, true) ? 1 : 0;
+    if (q_mapped && !p.q_mapped) return VA_ERR_INVALID;
     return launch_stream_fmt_g<1>(fmt, p, D, st);
 }
 
@@ -844,7 +857,13 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
     if (rc) return rc;
     const size_t bytes = (size_t)H * D * sizeof(__half);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The tile kernel loads the query from the mapped pinned buffer itself (one
+    // launch per step); other kernels get it copied into bufs->q first.
+    const bool direct = decode_uses_tile_kernel(fmt, H, L, D, ws_bytes >= va_workspace_bytes(H, D, S));
+    va_bufs b3 = b2;
+    b3.q = q_dev;
     const auto step = [&]() -> int {
+        if (direct) return decode_impl(fmt, &b3, H, L, D, S, ws, ws_bytes, nullptr, st, 1);
         int r = va_copy_small(const_cast<void*>(bufs->q), q_dev, bytes, st);
         if (!r) r = decode_impl(fmt, &b2, H, L, D, S, ws, ws_bytes, nullptr, st);
         return r;
