@@ -228,12 +228,15 @@ VA_API int va_copy_small(void* dst, const void* src, size_t bytes, void* stream)
  * reference counterpart; the reference's launch takes device buffers only):
  * copies q_host [H][D] fp16 into bufs->q, runs va_decode with its output
  * stored straight into out_host (bufs->out is not used), and returns once
- * out_host holds the result (it synchronizes the stream). Arguments as for
- * va_decode; q_host, out_host and bufs->q 16-byte aligned. On a created stream the three launches are captured into a
- * CUDA graph on the first call with a given argument set and replayed on later
- * calls with the same set (up to 16 sets cached, oldest dropped). The first
- * call therefore captures: make it outside any other stream capture. On the
- * legacy default stream (stream = NULL) the launches are made directly. */
+ * out_host holds the result (it synchronizes the stream). Arguments as for va_decode;
+ * q_host, out_host and bufs->q 16-byte aligned; q_host and out_host pinned
+ * and mapped (pageable memory returns VA_ERR_INVALID). On a created stream
+ * the launches are captured into a CUDA graph on the first call with a given
+ * argument set and replayed on later calls with the same set (up to 16 sets
+ * cached, oldest dropped; the pointers are validated when the set is first
+ * seen). The first call therefore captures: make it outside any other stream
+ * capture. On the legacy default stream (stream = NULL) the launches are
+ * made directly. */
 VA_API int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_host, int H, int L, int D,
                           int S, void* ws, size_t ws_bytes, void* stream);
 

@@ -78,9 +78,6 @@ struct DecodeParams {
     // KV stream are (query head, token) pairs, mq tokens per head; token i of
     // mq sees the stream's rows [0, len - (mq - 1 - i)) (1: plain decode)
     int mq;
-    // 1: q is pinned host memory mapped into the device (tile kernels: the
-    // producer loads it with plain loads instead of a bulk copy)
-    int q_mapped;
     // split-L across GPUs fused into the decode (xR > 0, tile kernel): the
     // head's merged partial is exchanged with the other ranks over peer
     // memory and the R partials merged into out (peer.cuh)

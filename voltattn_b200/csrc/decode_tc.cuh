@@ -280,31 +280,14 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
     const uint64_t pol = l2_policy_evict_first();
     // the first unit's query goes to its own buffer ahead of the tiles, so the
     // consumers prepare it while the tiles are in flight
-    // Query bytes of a stream and how they arrive: by bulk copy, or (p.q_mapped:
-    // the query sits in pinned host memory mapped into the device) by the
-    // lanes' plain loads, issued before the barrier arrival that publishes them.
-    constexpr uint32_t kQHeads = (uint32_t)C::kG * C::kD * 2;  // the stream's query heads
-    const uint32_t q_tx = p.q_mapped ? (uint32_t)C::kQBytes - kQHeads : (uint32_t)C::kQBytes;
-    const auto query_plain = [&](uint8_t* dst, int h) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.q + (size_t)h * C::kG * C::kD);
-        for (int i = lane; i < (int)kQHeads / 16; i += 32) {
-            uint4 v;
-            asm volatile("ld.global.cv.v4.u32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                         : "l"(src + 4 * i));
-            reinterpret_cast<uint4*>(dst)[i] = v;
-        }
-        __syncwarp();
-    };
     const auto first_query = [&]() {
-        const int h0 = (int)blockIdx.x / p.S;
-        if (p.q_mapped) query_plain(qfirst, h0);
         if (lane == 0) {
-            mbar_arrive_expect_tx(qbar, q_tx);
+            const int h0 = (int)blockIdx.x / p.S;
+            mbar_arrive_expect_tx(qbar, (uint32_t)C::kQBytes);
             if constexpr (C::kChan) {
-                if (!p.q_mapped) bulk_g2s(qfirst, p.q + (size_t)h0 * C::kD, C::kD * 2, qbar, pol);
+                bulk_g2s(qfirst, p.q + (size_t)h0 * C::kD, C::kD * 2, qbar, pol);
                 bulk_g2s(qfirst + C::kD * 2, p.scK + (size_t)h0 * C::kD, C::kD * 2, qbar, pol);
-            } else if (!p.q_mapped) {
+            } else {
                 bulk_g2s(qfirst, p.q + (size_t)h0 * C::kG * C::kD, (uint32_t)C::kQBytes, qbar, pol);
             }
         }
@@ -440,16 +423,13 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
             // a unit's first tile also carries the stream's query (and, with
             // per-channel K scales, the head's channel scales right after it);
             // the CTA's first unit has its query in its own buffer
-            const bool newq = t == 0 && u != (int)blockIdx.x;
-            const uint32_t qb = newq ? q_tx : 0u;  // query bytes by bulk copy
-            if (newq && p.q_mapped) query_plain(qring + stage * C::kQBytes, g.h);
+            const uint32_t qb = t == 0 && u != (int)blockIdx.x ? (uint32_t)C::kQBytes : 0u;
             const auto copy_query = [&]() {
                 if constexpr (C::kChan) {
-                    if (!p.q_mapped)
-                        bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kD, C::kD * 2, &full[stage], pol);
+                    bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kD, C::kD * 2, &full[stage], pol);
                     bulk_g2s(qring + stage * C::kQBytes + C::kD * 2, p.scK + (size_t)g.h * C::kD, C::kD * 2,
                              &full[stage], pol);
-                } else if (!p.q_mapped) {  // the stream's kG query heads, contiguous
+                } else {  // the stream's kG query heads, contiguous
                     bulk_g2s(qring + stage * C::kQBytes, p.q + (size_t)g.h * C::kG * C::kD, qb, &full[stage], pol);
                 }
             };
@@ -480,7 +460,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                     hdr[stage] = TcHeader{u, t, hnt, cur};
                     mbar_arrive_expect_tx(&full[stage],
                                           (uint32_t)nbox * C::kBox * (2u * C::kRb + C::kSbK + C::kSbV) + qb);
-                    if (newq) copy_query();
+                    if (qb) copy_query();
                     int seg = 0;  // first box of the current run of physically contiguous boxes
 #pragma unroll
                     for (int b = 0; b < C::kTr / C::kBox; ++b) {
@@ -518,7 +498,7 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                               : (uint32_t)nbox * C::kBox;
                 const uint32_t bytes = crows * 2u * C::kRb + (uint32_t)brows * (C::kSbK + C::kSbV) + qb;
                 mbar_arrive_expect_tx(&full[stage], bytes);
-                if (newq) copy_query();
+                if (qb) copy_query();
                 if constexpr (kFlatRows) {
                     if (crows > 0) {
                         bulk_g2s(sK, p.K + (size_t)t0 * C::kRb, crows * C::kRb, &full[stage], pol);

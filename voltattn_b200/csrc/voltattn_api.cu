@@ -100,7 +100,6 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     p.page_rows = 0;
     p.num_pages = 0;
     p.mq = 1;
-    p.q_mapped = 0;
     std::memset(&p.x, 0, sizeof(p.x));
     p.xR = 0;
     p.xrank = 0;
@@ -110,18 +109,8 @@ DecodeParams make_params(const va_bufs* b, int H, int L, int S, float* ws, unsig
     return p;
 }
 
-// Whether va_decode's fused path runs the tensor-core tile kernel for this
-// shape (the kernel that can take a query in mapped host memory).
-bool decode_uses_tile_kernel(int fmt, int H, int L, int D, bool fused) {
-    if (!fused || D != 128 || (long long)H * L >= (1ll << 31)) return false;
-    if (fmt == VA_Q4CP) return true;
-    if (fmt != VA_Q4P && fmt != VA_Q8P && fmt != VA_Q3P) return false;
-    const Kind kind = fmt == VA_Q4P ? Kind::Q4 : fmt == VA_Q8P ? Kind::Q8 : Kind::Q3;
-    return pick_consumer(kind, D, 1) == Consumer::kTc;
-}
-
 int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws, size_t ws_bytes, float* partial,
-                void* stream, int q_mapped = 0) {
+                void* stream) {
     int rc = check_decode_args(fmt, b, H, L, D, S);
     if (rc) return rc;
     if (!ws || !aligned16(ws) || ws_bytes < slots_bytes(H, D, S)) return VA_ERR_WORKSPACE;
@@ -135,8 +124,8 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
         if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;
         if ((long long)H * L >= (1ll << 31)) return VA_ERR_TOO_LARGE;
         unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
-        DecodeParams p = make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
-        p.q_mapped = q_mapped;
+        const DecodeParams p =
+            make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
         return launch_tc<TcCfg<Kind::Q4, 128, true>>(p, st);
     }
     if (is_plain(fmt) || !fused_ok) {
@@ -157,10 +146,8 @@ int decode_impl(int fmt, const va_bufs* b, int H, int L, int D, int S, void* ws,
         return VA_OK;
     }
     unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
-    DecodeParams p = make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
-    // a mapped-host query only where the tile kernel runs (its producer loads it)
-    p.q_mapped = q_mapped && decode_uses_tile_kernel(fmt, H, L, D, true) ? 1 : 0;
-    if (q_mapped && !p.q_mapped) return VA_ERR_INVALID;
+    const DecodeParams p =
+        make_params(b, H, L, S, slots, counters, partial ? kOutPartial : kOutHalf, partial);
     return launch_stream_fmt_g<1>(fmt, p, D, st);
 }
 
@@ -841,12 +828,41 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
                    void* ws, size_t ws_bytes, void* stream) {
     if (!bufs || !q_host || !out_host) return VA_ERR_INVALID;
     if (!aligned16(q_host) || !aligned16(out_host) || !aligned16(bufs->q)) return VA_ERR_ALIGN;
-    // the decode stores its output straight into out_host (mapped pinned
-    // memory takes plain global stores; the synchronize below makes them
-    // visible to the host); the query is copied in first, since the tile
-    // kernels bulk-copy it
-    // pageable host memory is rejected here, before any launch: a kernel
-    // cannot reach it (cached graphs below were built from validated pointers)
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // A created stream replays the graph cached for this argument set; it was
+    // built from pointers validated below on the first call with them.
+    HostStepKey key;
+    std::memset(&key, 0, sizeof(key));
+    if (st) {
+        int rc = current_device(&key.dev);
+        if (rc) return rc;
+        key.fmt = fmt;
+        key.H = H;
+        key.L = L;
+        key.D = D;
+        key.S = S;
+        key.b = *bufs;
+        key.q_host = q_host;
+        key.out_host = out_host;
+        key.ws = ws;
+        key.ws_bytes = ws_bytes;
+        key.st = st;
+        GraphExecRef cached;
+        {
+            std::lock_guard<std::mutex> lock(g_host_step_mu);
+            for (const auto& g : g_host_steps)
+                if (g.key == key) cached = g.exec;
+        }
+        if (cached) {
+            VA_CUDA(cudaGraphLaunch(cached.get(), st));
+            VA_CUDA(cudaStreamSynchronize(st));
+            return VA_OK;
+        }
+    }
+    // Pageable host memory is rejected here, before any launch: a kernel cannot
+    // reach it. The decode stores its output straight into out_host (mapped
+    // pinned memory takes plain global stores; the synchronize below makes
+    // them visible to the host).
     void *q_dev = nullptr, *out_dev = nullptr;
     int rc = device_view(q_host, &q_dev);
     if (!rc) rc = device_view(out_host, &out_dev);
@@ -856,14 +872,10 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
     rc = check_decode_args(fmt, &b2, H, L, D, S);
     if (rc) return rc;
     const size_t bytes = (size_t)H * D * sizeof(__half);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // The tile kernel loads the query from the mapped pinned buffer itself (one
-    // launch per step); other kernels get it copied into bufs->q first.
-    const bool direct = decode_uses_tile_kernel(fmt, H, L, D, ws_bytes >= va_workspace_bytes(H, D, S));
-    va_bufs b3 = b2;
-    b3.q = q_dev;
+    // q_host is copied into bufs->q by one small kernel (the decode kernels
+    // bulk-copy the query from device memory; 288 CTAs loading it from host
+    // memory themselves measured 51 against 34 us per step)
     const auto step = [&]() -> int {
-        if (direct) return decode_impl(fmt, &b3, H, L, D, S, ws, ws_bytes, nullptr, st, 1);
         int r = va_copy_small(const_cast<void*>(bufs->q), q_dev, bytes, st);
         if (!r) r = decode_impl(fmt, &b2, H, L, D, S, ws, ws_bytes, nullptr, st);
         return r;
@@ -874,35 +886,9 @@ int va_decode_host(int fmt, const va_bufs* bufs, const void* q_host, void* out_h
         VA_CUDA(cudaStreamSynchronize(st));
         return VA_OK;
     }
-    HostStepKey key;
-    std::memset(&key, 0, sizeof(key));
-    rc = current_device(&key.dev);
-    if (rc) return rc;
-    key.fmt = fmt;
-    key.H = H;
-    key.L = L;
-    key.D = D;
-    key.S = S;
-    key.b = *bufs;
-    key.q_host = q_host;
-    key.out_host = out_host;
-    key.ws = ws;
-    key.ws_bytes = ws_bytes;
-    key.st = st;
-    GraphExecRef cached;
-    {
-        std::lock_guard<std::mutex> lock(g_host_step_mu);
-        for (const auto& g : g_host_steps)
-            if (g.key == key) cached = g.exec;
-    }
-    if (cached) {
-        VA_CUDA(cudaGraphLaunch(cached.get(), st));
-        VA_CUDA(cudaStreamSynchronize(st));
-        return VA_OK;
-    }
     cudaGraphExec_t exec = nullptr;
     // first call with these arguments: run directly (also the warm-up of the
-    // decode's one-time set-up), then capture the same three launches
+    // decode's one-time set-up), then capture the same launches
     rc = step();
     if (rc) return rc;
     VA_CUDA(cudaStreamSynchronize(st));
