@@ -306,9 +306,11 @@ VA_API int va_decode_multiquery(int fmt, const va_bufs* bufs, const int* lens, i
  * (device int32 [B][max_pages]) at row j % page_rows. lens: device int32 [B],
  * 1 <= lens[b] <= max_pages * page_rows. Entries outside [0, num_pages) read
  * page 0 (decode) or skip the row (append). Decode supports every "+" format
- * but q4c+ at D = 64 or 128 with Hq / Hkv in {1, 2, 4, 8} and page_rows a
- * multiple of 8: q3+ / q4+ / q8+ with Hq == Hkv and q4+ with Hq == 2, 4 or
- * 8 * Hkv at D = 128 with page_rows a multiple of 32 run the tensor-core tile
+ * at D = 64 or 128 with Hq / Hkv in {1, 2, 4, 8} and page_rows a multiple of
+ * 8, and q4c+ with Hq == Hkv at D = 128 (its V row scales paged like the
+ * rows, its K channel scales [B][Hkv][D] per sequence, not paged): q3+ / q4+
+ * / q8+ / q4c+ with Hq == Hkv and q4+ with Hq == 2, 4 or 8 * Hkv at D = 128
+ * with page_rows a multiple of 32 run the tensor-core tile
  * kernels (splits s of a sequence take its 256-row tiles s, s + S, s + 2S,
  * ...); the rest the streaming / grouped-query kernels, which copy each run
  * of rows inside one page. Other shapes return VA_ERR_UNSUPPORTED. q must be
@@ -340,7 +342,9 @@ VA_API int va_probe_ceiling_method(int device, int method, size_t bytes, int rep
  * (G = Hq/Hkv in {1, 2, 4, 8}; "+" formats only). S = splits per sequence:
  * positions [s*c, (s+1)*c) with c = Lmax/S rounded up to 8 (splits past
  * lens[b] are empty). ws_bytes >= va_gqa_workspace_bytes(B, Hq, D, S), zeroed
- * before first use like va_decode's workspace. */
+ * before first use like va_decode's workspace. q4c+: Hq == Hkv and D = 128,
+ * K channel scales [B][Hkv][D] (va_quantize_kchan with H = B*Hkv, L = Lmax),
+ * V row scales [B][Hkv][Lmax], q 16-byte aligned. */
 VA_API size_t va_gqa_workspace_bytes(int B, int Hq, int D, int S);
 VA_API int va_decode_gqa(int fmt, const va_bufs* bufs, const int* lens, int B, int Hq, int Hkv, int Lmax,
                          int D, int S, void* ws, size_t ws_bytes, void* stream);

@@ -83,3 +83,60 @@ def test_q4c_rejects(va):
     with pytest.raises(RuntimeError):  # slots-only workspace (two-launch mode): not supported
         va.decode("q4c+", K, K, sK, sV, q, H, L, D, S, ws=torch.zeros(H * S * (D + 2), dtype=torch.float32,
                                                                           device="cuda"))
+
+
+@pytest.mark.parametrize("paged", [False, True], ids=["batched", "paged"])
+def test_decode_q4c_batched_and_paged(va, oracle, paged):
+    """q4c+ over a batch of sequences with their own lengths (one query head
+    per KV head), contiguous [B][Hkv][Lmax] or in a page pool (V row scales
+    paged with the rows, K channel scales per sequence and KV head); unused
+    pool rows carry nan V scales."""
+    import torch
+    B, Hkv, Lmax, D, S, P = 3, 4, 700, 128, 3, 64
+    rng = np.random.default_rng(11 + paged)
+    lens = rng.integers(1, Lmax + 1, size=B).astype(np.int32)
+    lens[0] = Lmax
+    streams = B * Hkv
+    kx = outlier_input(streams, Lmax, D, 5, edge=False)
+    vx = rng.standard_normal(streams * Lmax * D).astype(np.float32)
+    kc, ks = oracle.quantize_kchan(kx, streams, Lmax, D, 4)
+    vc, vs = oracle.quantize_vtok(vx, streams, Lmax, D, 4)
+    kd = oracle.dequant_kchan(kc, ks, streams, Lmax, D, 4)
+    vd = oracle.dequant_vtok(vc, vs, streams, Lmax, D, 4)
+    q = oracle.f2h(rng.standard_normal(B * Hkv * D).astype(np.float32))
+    ref = oracle.reference_gqa(kd, vd, q, lens, B, Hkv, Hkv, Lmax, D)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    qd = dev(q).view(torch.float16)
+    out = torch.full((B * Hkv * D,), float("nan"), dtype=torch.float16, device="cuda")
+    ws = torch.zeros(va.gqa_workspace_bytes(B, Hkv, D, S), dtype=torch.uint8, device="cuda")
+    if not paged:
+        b = va.DeviceBufs(dev(kc), dev(vc), dev(ks).view(torch.float16), dev(vs).view(torch.float16), qd, out, ws)
+        va.decode_gqa("q4c+", b, dev(lens), B, Hkv, Hkv, Lmax, D, S)
+    else:
+        max_pages = (Lmax + P - 1) // P
+        need = [(int(l) + P - 1) // P for l in lens]
+        num_pages = sum(need) + 3
+        perm = rng.permutation(num_pages)
+        table = np.zeros((B, max_pages), np.int32)
+        pk = rng.integers(0, 256, size=(num_pages, Hkv, P, D // 2), dtype=np.uint8)
+        pv = rng.integers(0, 256, size=(num_pages, Hkv, P, D // 2), dtype=np.uint8)
+        psv = np.full((num_pages, Hkv, P), np.float16(np.nan)).view(np.uint16)
+        k3, v3 = kc.reshape(B, Hkv, Lmax, D // 2), vc.reshape(B, Hkv, Lmax, D // 2)
+        s3 = vs.reshape(B, Hkv, Lmax)
+        i = 0
+        for bb in range(B):
+            for j in range(need[bb]):
+                pg = perm[i]
+                i += 1
+                table[bb, j] = pg
+                r0, r1 = j * P, min((j + 1) * P, int(lens[bb]))
+                pk[pg, :, :r1 - r0] = k3[bb, :, r0:r1]
+                pv[pg, :, :r1 - r0] = v3[bb, :, r0:r1]
+                psv[pg, :, :r1 - r0] = s3[bb, :, r0:r1]
+        b = va.DeviceBufs(dev(pk.ravel()), dev(pv.ravel()), dev(ks).view(torch.float16),
+                          dev(psv.ravel()).view(torch.float16), qd, out, ws)
+        va.decode_paged("q4c+", b, dev(table), max_pages, dev(lens), B, Hkv, Hkv, P, num_pages, D, S)
+    torch.cuda.synchronize()
+    err = np.abs(out.float().cpu().numpy() - ref)
+    bad = ~(err <= ATOL + RTOL * np.abs(ref))
+    assert not bad.any(), f"{bad.sum()} bad, maxerr {np.nanmax(err):.3e}"

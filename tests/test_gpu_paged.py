@@ -184,7 +184,7 @@ def test_paged_rejects_unsupported(va):
     b = va.DeviceBufs(K, K, sK, sK, q, out, ws)
     with pytest.raises(RuntimeError):  # page rows not a multiple of 8
         va.decode_paged("q4+", b, bt, max_pages, lens, B, Hq, Hkv, 12, num_pages, D, 1)
-    with pytest.raises(RuntimeError):  # per-channel scales are per sequence, not paged
-        va.decode_paged("q4c+", b, bt, max_pages, lens, B, Hq, Hkv, 32, num_pages, D, 1)
+    with pytest.raises(RuntimeError):  # q4c+: one query head per KV head only
+        va.decode_paged("q4c+", b, bt, max_pages, lens, B, 2 * Hkv, Hkv, 32, num_pages, D, 1)
     with pytest.raises(RuntimeError):  # 3 query heads per KV head
         va.decode_paged("q8+", b, bt, max_pages, lens, B, 3 * Hkv, Hkv, 32, num_pages, D, 1)

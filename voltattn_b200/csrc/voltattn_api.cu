@@ -617,6 +617,12 @@ int va_decode_gqa(int fmt, const va_bufs* b, const int* lens, int B, int Hq, int
     p.Hkv = Hkv;
     p.lens = lens;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (fmt == VA_Q4CP) {  // the tile kernel with channel scales per stream ([B*Hkv][D]), one query head each
+        if (G != 1 || D != 128) return VA_ERR_UNSUPPORTED;
+        if ((reinterpret_cast<uintptr_t>(b->q) & 15u) != 0) return VA_ERR_ALIGN;
+        if (p.total_rows >= (1ll << 31)) return VA_ERR_TOO_LARGE;
+        return launch_tc<TcCfg<Kind::Q4, 128, true>>(p, st);
+    }
     switch (G) {
         case 1: return launch_stream_fmt_g<1>(fmt, p, D, st);
         case 2: return launch_stream_fmt_g<2>(fmt, p, D, st);
@@ -664,7 +670,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     // with 2, 4 or 8; copy boxes of 32 rows stay inside a page
     const Kind kind = fmt == VA_Q8P ? Kind::Q8 : fmt == VA_Q3P ? Kind::Q3 : Kind::Q4;
     const bool tc = D == 128 && page_rows % 32 == 0 &&
-                    ((G == 1 && (fmt == VA_Q3P || fmt == VA_Q4P || fmt == VA_Q8P)) ||
+                    ((G == 1 && (fmt == VA_Q3P || fmt == VA_Q4P || fmt == VA_Q8P || fmt == VA_Q4CP)) ||
                      ((G == 2 || G == 4 || G == 8) && fmt == VA_Q4P)) &&
                     pick_consumer(kind, D, G) == Consumer::kTc;
     // every other "+" format and shape: the streaming / mma kernels, whose
@@ -703,6 +709,7 @@ int va_decode_paged(int fmt, const va_bufs* b, const int* block_table, int max_p
     if (G == 4) return launch_tcg<TcgCfg<Kind::Q4, 128, 4>>(p, st);
     if (G == 8) return launch_tcg<TcgCfg<Kind::Q4, 128, 8>>(p, st);
     if (fmt == VA_Q3P) return launch_tc<TcCfg<Kind::Q3, 128>>(p, st);
+    if (fmt == VA_Q4CP) return launch_tc<TcCfg<Kind::Q4, 128, true>>(p, st);  // V row scales paged, K per stream
     return fmt == VA_Q4P ? launch_tc<TcCfg<Kind::Q4, 128>>(p, st) : launch_tc<TcCfg<Kind::Q8, 128>>(p, st);
 }
 
