@@ -6,6 +6,9 @@
 #include "prefill_tc.cuh"
 
 namespace va {
+#ifdef PF_TIMELINE
+__device__ unsigned long long g_pf_tl[4096 * 8];
+#endif
 namespace host {
 
 template <class C>
@@ -111,3 +114,12 @@ int launch_prefill_fmt(int fmt, const PrefillParams& p, cudaStream_t st) {
 
 }  // namespace host
 }  // namespace va
+
+#ifdef PF_TIMELINE
+// Development builds only: per-CTA cycle totals of the staged prefill's phases.
+extern "C" int va_debug_pf_timeline(void* dst, size_t bytes) {
+    if (!dst || bytes < sizeof(va::g_pf_tl)) return VA_ERR_INVALID;
+    VA_CUDA(cudaMemcpyFromSymbol(dst, va::g_pf_tl, sizeof(va::g_pf_tl)));
+    return VA_OK;
+}
+#endif

@@ -732,6 +732,16 @@ __device__ __forceinline__ void pf_tma_2d(uint32_t dst, const CUtensorMap* map, 
 //   issue S(kb+1).
 // The copies land while the softmax runs; with two CTAs per SM the other
 // CTA's MMAs fill the tensor pipe meanwhile.
+#ifdef PF_TIMELINE
+extern __device__ unsigned long long g_pf_tl[4096 * 8];
+#define PF_T(v) v = clock64()
+#define PF_ACC(slot, a, b) \
+    do { if (tid == 0 && cta < 4096) acc[slot] += (unsigned long long)((b) - (a)); } while (0)
+#else
+#define PF_T(v) do { } while (0)
+#define PF_ACC(slot, a, b) do { } while (0)
+#endif
+
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, 2)
     prefill_tma_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmK,
@@ -825,11 +835,21 @@ __global__ void __launch_bounds__(C::kThreads, 2)
         k_pending = 0;
         if (!tfail) issue_s();
     }
+#ifdef PF_TIMELINE
+    const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+    unsigned long long acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#endif
     for (int kb = 0; kb < nkb; ++kb) {
         const long long r0 = (long long)kb * C::kBk;
         const bool more = kb + 1 < nkb;
+#ifdef PF_TIMELINE
+        long long c0, c1, c2, c3, c4, c5, c7, c9;
+#endif
+        PF_T(c0);
         // thread 0 gives up instead of waiting on an S that was never issued
         const bool ok_s = (tid == 0 && tfail) ? false : mbar_wait_bounded(bar_s, (uint32_t)kb & 1u);
+        PF_T(c1);
+        PF_ACC(0, c0, c1);
         if (!ok_s && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
         if (tid == 0 && ok_s && more) {  // the K tile is free: S(kb) has read it
@@ -861,10 +881,14 @@ __global__ void __launch_bounds__(C::kThreads, 2)
                 }
             }
             xch[hf * 128 + row] = fmaxf(bm0, bm1);
+            PF_T(c2);
+            PF_ACC(1, c1, c2);
             if (__syncthreads_or(!ok_s)) {
                 if (tid == 0) *fail = 1;
                 break;
             }
+            PF_T(c3);
+            PF_ACC(2, c2, c3);
             const float bm = fmaxf(xch[row], xch[128 + row]);
             const float bms = bm * qk_scale;
             const float mnew = bms > m + 8.f ? bms : m;
@@ -910,8 +934,12 @@ __global__ void __launch_bounds__(C::kThreads, 2)
                 tmem_wait_st();
             }
         }
+        PF_T(c4);
+        PF_ACC(3, c3, c4);
         tc05_fence_before();
         __syncthreads();
+        PF_T(c5);
+        PF_ACC(4, c4, c5);
         // O += P V once V(kb) has landed
         if (tid == 0) {
             if (!mbar_wait_bounded(bar_v, (uint32_t)kb & 1u)) tfail = true;
@@ -928,6 +956,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             }
         }
         const bool ok_o = (tid == 0 && tfail) ? false : mbar_wait_bounded(bar_o, (uint32_t)kb & 1u);
+        PF_T(c7);
+        PF_ACC(5, c5, c7);
         if (!ok_o && lane == 0) report_error(kErrFullWait);
         tc05_fence_after();
         if (tid == 0 && ok_o && more) {
@@ -942,7 +972,14 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             if (tid == 0) *fail = 1;
             break;
         }
+        PF_T(c9);
+        PF_ACC(6, c7, c9);
+        PF_ACC(7, c0, c9);
     }
+#ifdef PF_TIMELINE
+    if (tid == 0 && cta < 4096)
+        for (int i = 0; i < 8; ++i) g_pf_tl[cta * 8 + i] = i == 7 ? (acc[7] | ((unsigned long long)nkb << 48)) : acc[i];
+#endif
     // no copy may still be writing this CTA's shared memory when it exits
     if (tid == 0) {
         if (k_pending) mbar_wait_bounded(bar_k, k_phase);
