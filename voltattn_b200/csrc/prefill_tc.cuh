@@ -861,8 +861,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
             const int lim = (int)max(-1ll, min(min(vis, (long long)p.L - 1) - r0, (long long)C::kBk - 1)) - 64 * hf;
             const bool full = lim >= 63;
             float bm0 = kNegMax, bm1 = kNegMax;
+            uint32_t s[2][32];  // this half row of S, kept in registers for the weights
             {
-                uint32_t s[2][32];
                 tmem_ld32_nowait(tS + lane_addr, s[0]);
                 tmem_ld32_nowait(tS + lane_addr + 32, s[1]);
                 tmem_wait_ld_only();
@@ -900,7 +900,8 @@ __global__ void __launch_bounds__(C::kThreads, 2)
 #pragma unroll
             for (int cb = 0; cb < 2; ++cb) {
                 float sv[32];
-                tmem_ld32(tS + lane_addr + 32 * cb, sv);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(s[cb][i]);
 #pragma unroll
                 for (int c4 = 0; c4 < 4; ++c4) {
 #pragma unroll
