@@ -153,9 +153,10 @@ VA_API int va_decode_partial(int fmt, const va_bufs* bufs, int H, int L, int D, 
  * host array of the R buffers' device addresses as seen by this process
  * (peer_buffers[rank] is the local one). One call per decode step, with
  * epoch = 1, 2, 3, ... the same on all ranks: stores this rank's partial
- * (float [H][D+2], from va_decode_partial) into every rank's buffer, raises
- * a per-head flag on each, waits (bounded, ~1 s, then va_device_error) for
- * all R ranks' partials, and writes the merged fp16 output [H][D]. R <= 8. */
+ * (float [H][D+2], from va_decode_partial) into every rank's buffer as
+ * 64-bit words tagged with the epoch, waits (bounded, ~1 s, then
+ * va_device_error) until every word of the R ranks' partials carries the
+ * epoch, and writes the merged fp16 output [H][D]. R <= 8. */
 VA_API size_t va_exchange_buffer_bytes(int R, int H, int D);
 VA_API int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
                                unsigned epoch, void* out, void* stream);

@@ -1025,8 +1025,12 @@ __device__ void tc_ticket_warp(const DecodeParams& p, const int* th, uint64_t* t
                 float ms, ls, od[D / 32];
                 tc_merge_slots<D / 32>(p.ws + hq * p.S * (D + 2), p.S, D, lane, ms, ls, od);
                 if (p.xR > 0) {  // split-L across GPUs: exchange, merge the ranks' partials, write out
-                    if (peer_exchange_head<D / 32>(p.x, p.xR, p.xrank, *shep, p.xwait_ns, p.H * C::kG, D, (int)hq,
-                                                   ms, ls, od, lane, 32, lane, [] { __syncwarp(); }, shok)) {
+                    if (lane == 0) VA_TL(14, global_timer_ns());  // timeline: 14 exchange entered
+                    const bool xok =
+                        peer_exchange_head<D / 32>(p.x, p.xR, p.xrank, *shep, p.xwait_ns, p.H * C::kG, D, (int)hq, ms,
+                                                   ls, od, lane, 32, lane, [] { __syncwarp(); }, shok);
+                    if (lane == 0) VA_TL(15, global_timer_ns());  // timeline: 15 exchange merged
+                    if (xok) {
 #pragma unroll
                         for (int j = 0; j < D / 32; ++j) p.out[hq * D + lane + 32 * j] = __float2half_rn(od[j]);
                     }

@@ -323,6 +323,14 @@ int va_combine_partials(const float* slots, int R, int H, int S, int D, void* ou
     return VA_OK;
 }
 
+namespace {
+// Bytes of a rank's epoch-tagged gather words [2][R][H][D+2] (peer.cuh),
+// rounded to 256.
+size_t gather_bytes(int R, int H, int D) {
+    return ((size_t)2 * R * H * (D + 2) * sizeof(unsigned long long) + 255) & ~(size_t)255;
+}
+}  // namespace
+
 int va_set_peer_wait_limit(double seconds) {
     if (!(seconds > 0.0) || seconds > 60.0) return VA_ERR_INVALID;
     g_peer_wait_ns.store((unsigned long long)(seconds * 1e9));
@@ -331,10 +339,9 @@ int va_set_peer_wait_limit(double seconds) {
 
 size_t va_exchange_buffer_bytes(int R, int H, int D) {
     if (R < 1 || R > kMaxRanks || H < 1 || D < 1) return 0;
-    // gather slots, flags, and a 256-byte block whose first word counts this
-    // rank's steps (va_decode_splitl with epoch 0)
-    const size_t g = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
-    return g + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255) + 256;
+    // epoch-tagged gather words, and a 256-byte block whose first word counts
+    // this rank's steps (va_decode_splitl with epoch 0)
+    return gather_bytes(R, H, D) + 256;
 }
 
 int va_exchange_combine(const float* partial, int H, int D, int R, int rank, void* const* peer_buffers,
@@ -342,12 +349,10 @@ int va_exchange_combine(const float* partial, int H, int D, int R, int rank, voi
     if (!partial || !peer_buffers || !out || R < 1 || R > kMaxRanks || rank < 0 || rank >= R || H < 1 || D < 1 ||
         D > 128 || epoch == 0)
         return VA_ERR_INVALID;
-    const size_t goff = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
     PeerBuffers pb = {};
     for (int r = 0; r < R; ++r) {
         if (!peer_buffers[r] || !aligned16(peer_buffers[r])) return VA_ERR_INVALID;
-        pb.gather[r] = static_cast<float*>(peer_buffers[r]);
-        pb.flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[r]) + goff);
+        pb.gather[r] = static_cast<unsigned long long*>(peer_buffers[r]);
     }
     exchange_combine_kernel<<<H, 128, 0, static_cast<cudaStream_t>(stream)>>>(
         partial, H, D, R, rank, pb, epoch, g_peer_wait_ns.load(), static_cast<__half*>(out));
@@ -368,19 +373,15 @@ int va_decode_splitl(int fmt, const va_bufs* bufs, int H, int L, int D, int S, v
     if (!ws || !aligned16(ws) || ws_bytes < va_workspace_bytes(H, D, S)) return VA_ERR_WORKSPACE;
     unsigned* counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + counters_offset(H, D, S));
     DecodeParams p = make_params(bufs, H, L, S, static_cast<float*>(ws), counters, kOutHalf, nullptr);
-    const size_t goff = ((size_t)2 * R * H * (D + 2) * sizeof(float) + 255) & ~(size_t)255;
     for (int r = 0; r < R; ++r) {
         if (!peer_buffers[r] || !aligned16(peer_buffers[r])) return VA_ERR_INVALID;
-        p.x.gather[r] = static_cast<float*>(peer_buffers[r]);
-        p.x.flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[r]) + goff);
+        p.x.gather[r] = static_cast<unsigned long long*>(peer_buffers[r]);
     }
     p.xR = R;
     p.xrank = rank;
     p.xepoch = epoch;
-    if (epoch == 0) {  // the step count lives in this rank's buffer, after the flags
-        const size_t eoff = goff + (((size_t)2 * R * H * sizeof(unsigned) + 255) & ~(size_t)255);
-        p.xepoch_ptr = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[rank]) + eoff);
-    }
+    if (epoch == 0)  // the step count lives in this rank's buffer, after the gather words
+        p.xepoch_ptr = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(peer_buffers[rank]) + gather_bytes(R, H, D));
     p.xwait_ns = g_peer_wait_ns.load();
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (fmt == VA_Q4P) return launch_tc<TcCfg<Kind::Q4, 128>>(p, st);

@@ -14,8 +14,8 @@ inside one GPU). Decode shards three ways:
   log-sum-exp combine (va_combine_partials) produces the output on every
   rank. This is the reference's split-L combine (src/voltattn.cu:651-672)
   lifted across GPUs. `SplitLPeer` replaces the NCCL gather by one fused
-  kernel over NVLink peer memory (plain stores into the peers' buffers plus
-  per-head flags, no TMA and no multicast).
+  kernel over NVLink peer memory (epoch-tagged 64-bit stores into the peers'
+  buffers, no flags, no TMA and no multicast).
 
 The local compute is injectable so that the collective orchestration can be
 tested on CPU with the gloo backend.
@@ -108,8 +108,8 @@ class SplitL:
 class SplitLPeer(SplitL):
     """SplitL whose partial exchange runs over NVLink peer memory instead of
     NCCL: one fused kernel per step (va_exchange_combine) stores this rank's
-    partials into every rank's buffer, raises per-head flags, waits for the
-    peers' partials and merges them. Buffers come from torch symmetric
+    partials into every rank's buffer as epoch-tagged words, waits until the
+    peers' words carry the step's epoch and merges them. Buffers come from torch symmetric
     memory (mapped into every rank's address space)."""
 
     def __init__(self, L_total: int, H: int, D: int, device, group=None):
