@@ -3,6 +3,7 @@
 #include <mutex>
 
 #include "launch.cuh"
+#include "prefill_pp.cuh"
 #include "prefill_tc.cuh"
 
 namespace va {
@@ -53,8 +54,8 @@ static int launch_prefill_staged(const PrefillParams& p, void* ws, cudaStream_t 
     if (!attr_set[dev]) {
         std::lock_guard<std::mutex> lock(mu);
         if (!attr_set[dev]) {
-            VA_CUDA(cudaFuncSetAttribute(prefill_tma_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes));
+            VA_CUDA(cudaFuncSetAttribute(prefill_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PpCfg::kSmemBytes));
             attr_set[dev] = true;
         }
     }
@@ -74,8 +75,9 @@ static int launch_prefill_staged(const PrefillParams& p, void* ws, cudaStream_t 
     if (rc) return rc;
     rc = encode_f16_rows_map(&tmV, stV, (long long)p.Hkv * Lpad, C::kBk);
     if (rc) return rc;
-    const dim3 grid((unsigned)((p.Lq + C::kBq - 1) / C::kBq), (unsigned)p.Hq);
-    prefill_tma_kernel<C><<<grid, C::kThreads, C::kSmemBytes, st>>>(p, tmK, tmV, Lpad);
+    // pairs of 128-token tiles, one CTA per SM
+    const dim3 grid((unsigned)((p.Lq + 2 * PpCfg::kBq - 1) / (2 * PpCfg::kBq)), (unsigned)p.Hq);
+    prefill_pp_kernel<<<grid, PpCfg::kThreads, PpCfg::kSmemBytes, st>>>(p, tmK, tmV, Lpad);
     VA_CUDA(cudaGetLastError());
     return VA_OK;
 }
