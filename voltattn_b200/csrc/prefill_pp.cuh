@@ -40,9 +40,19 @@ namespace va {
 #ifdef PF_TIMELINE
 extern __device__ unsigned long long g_pf_tl[4096 * 8];
 #define PP_T(v) v = clock64()
+// event log of CTA (0, 0): region r (0: tile 0 softmax, 1: tile 1, 2: MMA
+// thread) of 8192 words: kind << 56 | kb << 40 | cycles since the start
+#define PP_EV(r, kind, kb)                                                                          \
+    do {                                                                                            \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && pp_nev < 8192)                                   \
+            g_pf_tl[(r) * 8192 + pp_nev++] = ((unsigned long long)(kind) << 56) |                   \
+                                             ((unsigned long long)(kb) << 40) |                     \
+                                             (unsigned long long)(clock64() - tstart);              \
+    } while (0)
 #define PP_ACC(slot, a, b) do { pp_acc[slot] += (unsigned long long)((b) - (a)); } while (0)
 #else
 #define PP_T(v) do { } while (0)
+#define PP_EV(r, kind, kb) do { } while (0)
 #define PP_ACC(slot, a, b) do { } while (0)
 #endif
 
@@ -66,6 +76,52 @@ __device__ __forceinline__ void tmem_st16_u(uint32_t taddr, const uint32_t* r) {
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+
+// 8 consecutive fp32 columns of this thread's TMEM lane (with the wait), and
+// the store back.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+                 : "memory");
+}
+
+// Bounded wait of the issue threads, which sit on the critical path of every
+// hand-off: try_wait without a suspend-time hint. (With the 20 us hint of
+// mbar_wait_bounded a wait took ~200 cycles even on a completed phase: 808
+// against 867 TFLOP/s; a test_wait spin took issue slots from the softmax
+// warps: 839.)
+__device__ __forceinline__ bool pp_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool pp_wait(uint64_t* bar, uint32_t parity) {
+    if (pp_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (pp_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 
 __global__ void __launch_bounds__(PpCfg::kThreads, 1)
@@ -129,6 +185,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
     unsigned long long pp_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     long long t0, t1, t2, t3, t4;
     const long long tstart = clock64();
+    int pp_nev = 0;
 #endif
 
     if (warp == 9) {
@@ -140,7 +197,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             int n = 0;
             for (; n < nitems; ++n) {
                 const int slot = n % C::kRing;
-                if (n >= C::kRing && !mbar_wait_bounded(&freeb[slot], (uint32_t)(n / C::kRing - 1) & 1u)) {
+                if (n >= C::kRing && !pp_wait(&freeb[slot], (uint32_t)(n / C::kRing - 1) & 1u)) {
                     report_error(kErrEmptyWait);
                     break;
                 }
@@ -165,7 +222,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             bool ok = true;
             const auto wait_item = [&](int n) {
                 PP_T(t2);
-                const bool got = ok && mbar_wait_bounded(&full[n % C::kRing], (uint32_t)(n / C::kRing) & 1u);
+                const bool got = ok && pp_wait(&full[n % C::kRing], (uint32_t)(n / C::kRing) & 1u);
                 PP_T(t3);
                 PP_ACC(6, t2, t3);
                 if (ok && !got) {
@@ -195,7 +252,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             };
             const auto wait_p = [&](int w, int kb) {
                 PP_T(t0);
-                const bool got = ok && mbar_wait_bounded(&pready[w], (uint32_t)kb & 1u);
+                const bool got = ok && pp_wait(&pready[w], (uint32_t)kb & 1u);
                 PP_T(t1);
                 PP_ACC(4 + w, t0, t1);
                 if (ok && !got) {
@@ -213,24 +270,32 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             for (int kb = 0; ok && kb < nkb1; ++kb) {
                 bool v_waited = false, k_waited = false;
                 if (kb < nkb0) {
-                    if (!wait_p(0, kb) || !wait_item(2 * kb + 1)) break;
+                    if (!wait_p(0, kb)) break;
+                    PP_EV(2, 11, kb);
+                    if (!wait_item(2 * kb + 1)) break;
                     v_waited = true;
+                    PP_EV(2, 5, kb);
                     issue_pv(0, kb);
                     if (kb == nkb0 - 1) umma_commit(&odone[0]);
                     if (kb + 1 < nkb0) {
+                        PP_EV(2, 12, kb);
                         if (!wait_item(2 * kb + 2)) break;
+                        PP_EV(2, 13, kb);
                         k_waited = true;
                         issue_s(0, kb + 1);
+                        PP_EV(2, 7, kb);
                     }
                 }
                 if (!wait_p(1, kb)) break;
                 if (!v_waited && !wait_item(2 * kb + 1)) break;
+                PP_EV(2, 8, kb);
                 issue_pv(1, kb);
                 umma_commit(&freeb[(2 * kb + 1) % C::kRing]);
                 if (kb == nkb1 - 1) umma_commit(&odone[1]);
                 if (kb + 1 < nkb1) {
                     if (!k_waited && !wait_item(2 * kb + 2)) break;
                     issue_s(1, kb + 1);
+                    PP_EV(2, 10, kb);
                     umma_commit(&freeb[(2 * kb + 2) % C::kRing]);
                 }
             }
@@ -239,9 +304,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             mbar_wait_bounded(fin, 0);
 #ifdef PF_TIMELINE
             const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
-            if (cta < 4096)
-                for (int i = 4; i < 7; ++i) g_pf_tl[cta * 8 + i] = pp_acc[i];
-            if (cta < 4096) g_pf_tl[cta * 8 + 7] = (unsigned long long)(clock64() - tstart) | ((unsigned long long)nkb1 << 48);
+            (void)cta;
 #endif
         }
     } else {
@@ -261,6 +324,7 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             const bool got_s = mbar_wait_bounded(&sfull[w], (uint32_t)kb & 1u);
             PP_T(t1);
             PP_ACC(0, t0, t1);
+            PP_EV(w, 1, kb);
             if (!got_s) {
                 if (lane == 0) report_error(kErrFullWait);
                 ok = false;
@@ -297,6 +361,18 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
             const float mnew = bms > m + 8.f ? bms : m;
             const float corr = fast_exp2(m - mnew);
             m = mnew;
+            // O_w has no MMA in flight here (S_w(kb) completed after PV_w(kb-1)):
+            // rescale it before P(kb) lets PV start
+            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+                for (int c = 0; c < 16; ++c) {
+                    float o[8];
+                    tmem_ld8(tO + 8u * c, o);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] *= corr;
+                    tmem_st8(tO + 8u * c, o);
+                }
+            }
             float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};  // 4 chains: the adds do not serialize
             const float2 sc2 = make_float2(qk_scale, qk_scale), nm2 = make_float2(-mnew, -mnew);
@@ -315,32 +391,22 @@ __global__ void __launch_bounds__(PpCfg::kThreads, 1)
                 }
                 tmem_st16_u(tS + 16u * c, pw);
             }
+            // P(kb) written: this tile's PV may start
+            tmem_wait_st();
+            tc05_fence_before();
+            mbar_arrive(&pready[w]);
+            if ((tid & 127) == 0) PP_EV(w, 2, kb);
             const float2 sa = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
             l = l * corr + (sa.x + sa.y);
             PP_T(t3);
             PP_ACC(2, t2, t3);
-            // O_w has no MMA in flight here (S_w(kb) completed after PV_w(kb-1))
-            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float o[32];
-                    tmem_ld32(tO + 32u * c, o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
-                    tmem_st32(tO + 32u * c, o);
-                }
-            }
-            tmem_wait_st();
-            tc05_fence_before();
-            mbar_arrive(&pready[w]);
             PP_T(t4);
             PP_ACC(3, t3, t4);
         }
 #ifdef PF_TIMELINE
         if (tid == 0) {
             const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
-            if (cta < 4096)
-                for (int i = 0; i < 4; ++i) g_pf_tl[cta * 8 + i] = pp_acc[i];
+            (void)cta;
         }
 #endif
         // epilogue: O_w / l -> out once the tile's last PV completed
