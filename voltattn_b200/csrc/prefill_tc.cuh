@@ -724,299 +724,4 @@ __device__ __forceinline__ void pf_tma_2d(uint32_t dst, const CUtensorMap* map, 
         : "memory");
 }
 
-// The attention over the staging rows. Per block kb of 128 cache rows (one
-// thread issues every copy and MMA):
-//   wait S(kb); copy K(kb+1) (the K tile is free once S(kb) has read it);
-//   softmax(kb) by all 8 warps, P into TMEM (as in prefill_tc_kernel);
-//   wait V(kb), issue O += P V; wait PV(kb); copy V(kb+1); wait K(kb+1),
-//   issue S(kb+1).
-// The copies land while the softmax runs; with two CTAs per SM the other
-// CTA's MMAs fill the tensor pipe meanwhile.
-#ifdef PF_TIMELINE
-extern __device__ unsigned long long g_pf_tl[4096 * 8];
-#define PF_T(v) v = clock64()
-#define PF_ACC(slot, a, b) \
-    do { if (tid == 0 && cta < 4096) acc[slot] += (unsigned long long)((b) - (a)); } while (0)
-#else
-#define PF_T(v) do { } while (0)
-#define PF_ACC(slot, a, b) do { } while (0)
-#endif
-
-template <class C>
-__global__ void __launch_bounds__(C::kThreads, 2)
-    prefill_tma_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, int Lpad) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* sQ = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sK = sQ + C::kTile;
-    uint8_t* sV = sK + C::kTile;
-    uint64_t* bar_s = reinterpret_cast<uint64_t*>(sV + C::kTile);
-    uint64_t* bar_o = bar_s + 1;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
-    volatile int* fail = reinterpret_cast<volatile int*>(tslot + 1);
-    uint64_t* bar_k = bar_s + 4;
-    uint64_t* bar_v = bar_s + 5;
-    float* xch = reinterpret_cast<float*>(bar_s + 8);  // [2][128]: the half-rows' maxima / sums
-
-    constexpr int D = C::kD;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nqb = (int)gridDim.x;
-    const int qb = nqb - 1 - (int)blockIdx.x;  // the longest (last) token blocks start first
-    const int h = (int)blockIdx.y;
-    const int hk = h / (p.Hq / p.Hkv);
-    const int q0 = qb * C::kBq;
-    const long long off0 = (long long)p.L - p.Lq;  // cache row of token 0
-    const long long last = min((long long)p.L - 1, off0 + q0 + C::kBq - 1);
-    const int nkb = (int)(last / C::kBk) + 1;
-    const int ybase = hk * Lpad;  // staging row of the KV head's row 0
-    const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-    constexpr uint32_t kTileBytes = (uint32_t)C::kTile;
-
-    if (warp == 0) tmem_alloc(tslot, C::kTmemCols);
-    if (tid == 0) {
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
-        mbar_init(bar_k, 1);
-        mbar_init(bar_v, 1);
-        *fail = 0;
-        fence_mbar_init();
-        prefetch_tensormap(&tmK);
-        prefetch_tensormap(&tmV);
-    }
-    __syncthreads();
-    // tile kb of a matrix: two 64-dim boxes of 128 rows (panels 16 KB apart)
-    const auto copy_tile = [&](const CUtensorMap* map, uint32_t dst, uint64_t* bar, int kb) {
-        mbar_arrive_expect_tx(bar, kTileBytes);
-        pf_tma_2d(dst, map, 0, ybase + kb * C::kBk, bar);
-        pf_tma_2d(dst + 16384u, map, 64, ybase + kb * C::kBk, bar);
-    };
-    if (tid == 0) {
-        copy_tile(&tmK, sKa, bar_k, 0);
-        copy_tile(&tmV, sVa, bar_v, 0);
-    }
-    // this CTA's query tokens -> sQ (rows past Lq are zero)
-    for (int i = tid; i < C::kBq * 16; i += C::kThreads) {
-        const int r = i >> 4, c = i & 15;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (q0 + r < p.Lq)
-            v = __ldg(reinterpret_cast<const uint4*>(p.q + ((size_t)h * p.Lq + q0 + r) * D) + c);
-        sts128_generic(sQ, pf_off(r, c), v);
-    }
-    fence_proxy_async_smem();
-    tc05_fence_before();
-    __syncthreads();
-    tc05_fence_after();
-    const uint32_t tbase = *tslot;
-    const uint32_t tS = tbase, tO = tbase + 128;
-    constexpr uint32_t kIdescS = umma_idesc_f16(128, 128, false);
-    constexpr uint32_t kIdescO = umma_idesc_f16(128, 128, true);
-    const int hf = warp >> 2;
-    const int row = tid & 127;
-    const long long vis = off0 + q0 + row;  // last visible cache row of this token
-    const float qk_scale = rsqrtf((float)D) * kLog2e;
-    float m = kNegMax, l = 0.f;
-    const uint32_t lane_addr = ((uint32_t)((warp & 3) * 32) << 16) + 64 * hf;
-    // copies in flight (thread 0) and the phase each completes: waited for on
-    // every exit path
-    int k_pending = 1, v_pending = 1;
-    uint32_t k_phase = 0, v_phase = 0;
-    bool tfail = false;  // thread 0: a copy or MMA wait gave up
-    const auto issue_s = [&]() {  // S = Q K^T of the block in the K tile
-        tc05_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t o = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-            umma_f16(tS, umma_desc_sw128(sQa + o, 16, 1024), umma_desc_sw128(sKa + o, 16, 1024), kIdescS, kk > 0);
-        }
-        umma_commit(bar_s);
-    };
-    if (tid == 0) {
-        if (!mbar_wait_bounded(bar_k, 0)) tfail = true;
-        k_pending = 0;
-        if (!tfail) issue_s();
-    }
-#ifdef PF_TIMELINE
-    const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x);
-    unsigned long long acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#endif
-    for (int kb = 0; kb < nkb; ++kb) {
-        const long long r0 = (long long)kb * C::kBk;
-        const bool more = kb + 1 < nkb;
-#ifdef PF_TIMELINE
-        long long c0, c1, c2, c3, c4, c5, c7, c9;
-#endif
-        PF_T(c0);
-        // thread 0 gives up instead of waiting on an S that was never issued
-        const bool ok_s = (tid == 0 && tfail) ? false : mbar_wait_bounded(bar_s, (uint32_t)kb & 1u);
-        PF_T(c1);
-        PF_ACC(0, c0, c1);
-        if (!ok_s && lane == 0) report_error(kErrFullWait);
-        tc05_fence_after();
-        if (tid == 0 && ok_s && more) {  // the K tile is free: S(kb) has read it
-            copy_tile(&tmK, sKa, bar_k, kb + 1);
-            k_pending = 1;
-            k_phase = (uint32_t)(kb + 1) & 1u;
-        }
-        {
-            const int lim = (int)max(-1ll, min(min(vis, (long long)p.L - 1) - r0, (long long)C::kBk - 1)) - 64 * hf;
-            const bool full = lim >= 63;
-            float bm0 = kNegMax, bm1 = kNegMax;
-            uint32_t s[2][32];  // this half row of S, kept in registers for the weights
-            {
-                tmem_ld32_nowait(tS + lane_addr, s[0]);
-                tmem_ld32_nowait(tS + lane_addr + 32, s[1]);
-                tmem_wait_ld_only();
-                tmem_tie32(s[0]);
-                tmem_tie32(s[1]);
-#pragma unroll
-                for (int j = 0; j < 64; j += 2) {
-                    const float x0 = __uint_as_float(s[j >> 5][j & 31]), x1 = __uint_as_float(s[j >> 5][(j & 31) + 1]);
-                    if (full) {
-                        if (j & 2) bm1 = fmax3f(bm1, x0, x1);
-                        else bm0 = fmax3f(bm0, x0, x1);
-                    } else {
-                        if (j <= lim) bm0 = fmaxf(bm0, x0);
-                        if (j + 1 <= lim) bm1 = fmaxf(bm1, x1);
-                    }
-                }
-            }
-            xch[hf * 128 + row] = fmaxf(bm0, bm1);
-            PF_T(c2);
-            PF_ACC(1, c1, c2);
-            if (__syncthreads_or(!ok_s)) {
-                if (tid == 0) *fail = 1;
-                break;
-            }
-            PF_T(c3);
-            PF_ACC(2, c2, c3);
-            const float bm = fmaxf(xch[row], xch[128 + row]);
-            const float bms = bm * qk_scale;
-            const float mnew = bms > m + 8.f ? bms : m;
-            const float corr = fast_exp2(m - mnew);
-            m = mnew;
-            float2 sum2 = make_float2(0.f, 0.f);
-            uint32_t pw[32];
-            const float2 sc2 = make_float2(qk_scale, qk_scale), nm2 = make_float2(-mnew, -mnew);
-#pragma unroll
-            for (int cb = 0; cb < 2; ++cb) {
-                float sv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(s[cb][i]);
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int j = 32 * cb + 8 * c4 + 2 * i;
-                        const float2 x = ffma2(make_float2(sv[j & 31], sv[(j & 31) + 1]), sc2, nm2);
-                        float a = fast_exp2(x.x);
-                        float b = fast_exp2(x.y);
-                        if (!full) {
-                            a = j <= lim ? a : 0.f;
-                            b = j + 1 <= lim ? b : 0.f;
-                        }
-                        sum2 = fadd2(sum2, make_float2(a, b));
-                        const __half2 hp = __floats2half2_rn(a, b);
-                        pw[j >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
-                    }
-                }
-            }
-            tmem_st32_u(tS + lane_addr, pw);
-            tmem_wait_st();
-            l = l * corr + (sum2.x + sum2.y);
-            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll
-                for (int cb = 0; cb < 2; ++cb) {
-                    float o[32];
-                    tmem_ld32(tO + lane_addr + 32 * cb, o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
-                    tmem_st32(tO + lane_addr + 32 * cb, o);
-                }
-                tmem_wait_st();
-            }
-        }
-        PF_T(c4);
-        PF_ACC(3, c3, c4);
-        tc05_fence_before();
-        __syncthreads();
-        PF_T(c5);
-        PF_ACC(4, c4, c5);
-        // O += P V once V(kb) has landed
-        if (tid == 0) {
-            if (!mbar_wait_bounded(bar_v, (uint32_t)kb & 1u)) tfail = true;
-            v_pending = 0;
-            if (!tfail) {
-                tc05_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < C::kBk / 16; ++kk) {
-                    const uint32_t ta = tS + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
-                    const uint32_t ob = (uint32_t)(kk * 16 * 128);
-                    umma_f16_ts(tO, ta, umma_desc_sw128(sVa + ob, 16384, 1024), kIdescO, kb > 0 || kk > 0);
-                }
-                umma_commit(bar_o);
-            }
-        }
-        const bool ok_o = (tid == 0 && tfail) ? false : mbar_wait_bounded(bar_o, (uint32_t)kb & 1u);
-        PF_T(c7);
-        PF_ACC(5, c5, c7);
-        if (!ok_o && lane == 0) report_error(kErrFullWait);
-        tc05_fence_after();
-        if (tid == 0 && ok_o && more) {
-            copy_tile(&tmV, sVa, bar_v, kb + 1);  // the V tile is free: PV(kb) has read it
-            v_pending = 1;
-            v_phase = (uint32_t)(kb + 1) & 1u;
-            if (!mbar_wait_bounded(bar_k, (uint32_t)(kb + 1) & 1u)) tfail = true;
-            k_pending = 0;
-            if (!tfail) issue_s();
-        }
-        if (__syncthreads_or(!ok_o || (tid == 0 && tfail))) {
-            if (tid == 0) *fail = 1;
-            break;
-        }
-        PF_T(c9);
-        PF_ACC(6, c7, c9);
-        PF_ACC(7, c0, c9);
-    }
-#ifdef PF_TIMELINE
-    if (tid == 0 && cta < 4096)
-        for (int i = 0; i < 8; ++i) g_pf_tl[cta * 8 + i] = i == 7 ? (acc[7] | ((unsigned long long)nkb << 48)) : acc[i];
-#endif
-    // no copy may still be writing this CTA's shared memory when it exits
-    if (tid == 0) {
-        if (k_pending) mbar_wait_bounded(bar_k, k_phase);
-        if (v_pending) mbar_wait_bounded(bar_v, v_phase);
-    }
-    __syncthreads();
-    xch[hf * 128 + row] = l;
-    __syncthreads();
-    if (!*fail) {
-        const float inv = 1.f / (xch[row] + xch[128 + row]);
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            float o[32];
-            tmem_ld32(tO + lane_addr + 32 * cb, o);
-            if (q0 + row < p.Lq) {
-                uint4* dst =
-                    reinterpret_cast<uint4*>(p.out + ((size_t)h * p.Lq + q0 + row) * D + 64 * hf + 32 * cb);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const __half2 hp = __floats2half2_rn(o[8 * c + 2 * i] * inv, o[8 * c + 2 * i + 1] * inv);
-                        w[i] = *reinterpret_cast<const uint32_t*>(&hp);
-                    }
-                    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-        }
-    }
-    tc05_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc05_fence_after();
-        tmem_dealloc(tbase, C::kTmemCols);
-    }
-}
-
 }  // namespace va
