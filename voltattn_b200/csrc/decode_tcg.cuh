@@ -328,7 +328,7 @@ __device__ __forceinline__ void tcg_tile(uint32_t sK, uint32_t sV, const __half*
     __syncwarp();
 }
 
-template <class C>
+template <class C, bool kPaged>
 __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     decode_tcg_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV) {
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
         }
-        tc_producer<C>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar,
+        tc_producer<C, kPaged>(p, &tmK, &tmV, stages, hdr, qring, full, empty, qfirst, qbar,
                        reinterpret_cast<volatile unsigned*>(shFail + 2));
         return;
     }

@@ -15,10 +15,12 @@ static int tcg_ctas_per_sm(int dev, int* out) {
     if (occ[dev] == 0) {
         std::lock_guard<std::mutex> lock(mu);
         if (occ[dev] == 0) {
-            VA_CUDA(cudaFuncSetAttribute(decode_tcg_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            VA_CUDA(cudaFuncSetAttribute(decode_tcg_kernel<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes));
+            VA_CUDA(cudaFuncSetAttribute(decode_tcg_kernel<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes));
             int n = 0;
-            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tcg_kernel<C>, C::kThreads,
+            VA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_tcg_kernel<C, false>, C::kThreads,
                                                                   C::kSmemBytes));
             occ[dev] = std::max(1, n);
         }
@@ -51,7 +53,9 @@ int launch_tcg(const DecodeParams& p, cudaStream_t st) {
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tcg_kernel<C>, p, tmK, tmV));
+    // one instantiation per copy path (contiguous rows or a page pool)
+    if (p.page_rows > 0) VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tcg_kernel<C, true>, p, tmK, tmV));
+    else VA_CUDA(cudaLaunchKernelEx(&cfg, decode_tcg_kernel<C, false>, p, tmK, tmV));
     return VA_OK;
 }
 
