@@ -98,6 +98,9 @@ struct TcCfg {
     static constexpr int kRpw = 64;  // rows per warp per tile
     static constexpr int kTr = kWarps * kRpw;
     static constexpr int kBox = 32;  // rows per tensor copy
+    // rows per tensor copy of a contiguous cache (64 and 128 measured
+    // slower for batch-1 q4+ / q8+: 17.09 -> 17.29 / 17.34 us at L=16384)
+    static constexpr int kBoxC = 32;
     static constexpr int kThreads = (kWarps + 2) * 32;  // consumers, producer, ticket warp
     static constexpr int kStages = 3;
     static constexpr int kTRing = 4;  // finished units handed to the ticket warp
@@ -271,6 +274,13 @@ constexpr bool kTcEarlyKv = true;
 #else
 constexpr bool kTcEarlyKv = false;
 #endif
+
+// Rows per tensor copy of a contiguous cache (the paged path copies kBox-row
+// boxes, each inside one page; q3 rows move as flat byte ranges).
+template <class C>
+__host__ __device__ constexpr int tc_box_rows() {
+    return C::kKind == Kind::Q3 ? C::kBox : (C::kBoxC < C::kTr ? C::kBoxC : C::kTr);
+}
 
 // kPaged: the cache is a page pool (block table); a template parameter so
 // that each instantiation carries only one copy path: the producer's code
@@ -503,9 +513,11 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                 hdr[stage] = TcHeader{u, t, hnt, cur};
                 // flat codes: the tile's rows inside the tensor, one bulk copy
                 // per matrix (rows past the end stay stale; they are masked)
+                constexpr int kBx = tc_box_rows<C>();
+                const int nbx = (need + kBx - 1) / kBx;
                 const uint32_t crows =
                     kFlatRows ? (uint32_t)max(0ll, min((long long)nbox * C::kBox, p.total_rows - t0))
-                              : (uint32_t)nbox * C::kBox;
+                              : (uint32_t)nbx * kBx;
                 const uint32_t bytes = crows * 2u * C::kRb + (uint32_t)brows * (C::kSbK + C::kSbV) + qb;
                 mbar_arrive_expect_tx(&full[stage], bytes);
                 if (qb) copy_query();
@@ -515,10 +527,10 @@ __device__ void tc_producer(const DecodeParams& p, const CUtensorMap* tmK, const
                         bulk_g2s(sV, p.V + (size_t)t0 * C::kRb, crows * C::kRb, &full[stage], pol);
                     }
                 } else {
-                    for (int b = 0; b < nbox; ++b) {
-                        const int y = (int)(t0 + (long long)b * C::kBox);
-                        tma_load_2d(sK + b * C::kBox * C::kRb, tmK, 0, y, &full[stage], pol);
-                        tma_load_2d(sV + b * C::kBox * C::kRb, tmV, 0, y, &full[stage], pol);
+                    for (int b = 0; b < nbx; ++b) {
+                        const int y = (int)(t0 + (long long)b * kBx);
+                        tma_load_2d(sK + b * kBx * C::kRb, tmK, 0, y, &full[stage], pol);
+                        tma_load_2d(sV + b * kBx * C::kRb, tmV, 0, y, &full[stage], pol);
                     }
                 }
                 if (brows > 0) {

@@ -52,6 +52,8 @@ struct TcgCfg {
     static constexpr int kRpw = 64;
     static constexpr int kTr = kRowWarps * kRpw;
     static constexpr int kBox = 32;
+    // rows per tensor copy of a contiguous cache: 128 (config 5: 0.266 -> 0.260 ms against 32)
+    static constexpr int kBoxC = 128;
     static constexpr int kThreads = (kWarps + 2) * 32;
     static constexpr int kMinBlocks = kHg == 1 ? 2 : 1;  // CTAs per SM the smem budget is cut for
     static constexpr int kStages = kHg == 1 ? 3 : 5;

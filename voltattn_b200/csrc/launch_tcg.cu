@@ -37,9 +37,11 @@ int launch_tcg(const DecodeParams& p, cudaStream_t st) {
     rc = tcg_ctas_per_sm<C>(dev, &occ);
     if (rc) return rc;
     CUtensorMap tmK, tmV;
-    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, C::kBox);
+    // copy boxes: kBox rows inside a page, kTcBoxC rows of a contiguous cache
+    const int box = p.page_rows > 0 ? C::kBox : tc_box_rows<C>();
+    rc = encode_rows_map(&tmK, p.K, p.total_rows, C::kRb, box);
     if (rc) return rc;
-    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, C::kBox);
+    rc = encode_rows_map(&tmV, p.V, p.total_rows, C::kRb, box);
     if (rc) return rc;
     const long long units = (long long)p.H * p.S;
     const int grid = (int)std::min<long long>(units, (long long)sm_count(dev) * occ);
