@@ -41,8 +41,8 @@ FORMAT_BITS = {"f16": 16, "f16+": 16, "q8": 8, "q8+": 8, "q4": 4, "q4+": 4, "q3+
 # and scaled to L=16384 by the rows processed (x 1/4): traffic grows in
 # proportion to the rows, and the reads equal the algorithmic bytes there.
 # Formats without a capture report None.
-NCU_TRAFFIC_BYTES = {"q4+": int((285.285120e6 + 3.214080e6) / 4),
-                     "q8+": int((553.715456e6 + 3.673344e6) / 4),
+NCU_TRAFFIC_BYTES = {"q4+": int((285.290496e6 + 3.848704e6) / 4),
+                     "q8+": int((553.788672e6 + 5.725184e6) / 4),
                      "f16+": int((1073.790e6 + 3.593472e6) / 4)}
 
 
